@@ -1,0 +1,112 @@
+// common.cuh — shared helpers of libgsec: error reporting, 16-byte vector
+// access, launch sizing and GF(2^8)/GF(2^16) arithmetic.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/gsec.h"
+
+namespace gsec {
+
+// ---------------------------------------------------------------- errors ----
+
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+#define GSEC_REQUIRE(cond, ...)               \
+  do {                                        \
+    if (!(cond)) {                            \
+      ::gsec::set_error(__VA_ARGS__);         \
+      return GSEC_EINVAL;                     \
+    }                                         \
+  } while (0)
+
+// Returns GSEC_ECUDA with the launch error if the last launch failed.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(gsec_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------- vector access ---
+
+// 16-byte global load that bypasses L1 allocation: every byte of a shard is
+// read once, so caching it in L1 only evicts useful lines.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// 16-byte global load through the coherent path (peer memory written by another
+// GPU during this kernel's lifetime is not assumed; used where the read-only
+// path would be unsafe because the same buffer is written by the kernel).
+__device__ __forceinline__ uint4 ld_plain(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+// 16-byte streaming store (evict-first: parity is not re-read by this kernel).
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 vxor(uint4 a, uint4 b) {
+  return make_uint4(a.x ^ b.x, a.y ^ b.y, a.z ^ b.z, a.w ^ b.w);
+}
+
+__device__ __forceinline__ uint4 vzero() { return make_uint4(0u, 0u, 0u, 0u); }
+
+// ------------------------------------------------------------- GF(2^8) ------
+// Field GF(2)[x]/(x^8+x^4+x^3+x^2+1) (0x11d), generator x (= 2).
+
+__host__ __device__ __forceinline__ uint32_t gf8_mul(uint32_t a, uint32_t b) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (b & 1u) r ^= a;
+    b >>= 1;
+    a <<= 1;
+    if (a & 0x100u) a ^= 0x11du;
+  }
+  return r & 0xffu;
+}
+
+// ------------------------------------------------------------ GF(2^16) ------
+// Field GF(2)[x]/(x^16+x^12+x^3+x+1) (0x1100B), generator x, as built by the
+// reference's init_gf_tables (benchmark/rs/main.py:39-54).
+
+__host__ __device__ __forceinline__ uint32_t gf16_mul(uint32_t a, uint32_t b) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (b & 1u) r ^= a;
+    b >>= 1;
+    a <<= 1;
+    if (a & 0x10000u) a ^= 0x1100bu;
+  }
+  return r & 0xffffu;
+}
+
+// Host-side tables and inverses (defined in gf.cpp part of api.cu).
+uint8_t gf8_inv(uint8_t a);
+uint16_t gf16_exp(int e);          // alpha^e, e in [0, 2*65535)
+uint16_t gf16_log(uint16_t a);     // discrete log, a != 0
+uint16_t gf16_mul_tab(uint16_t a, uint16_t b);  // exp/log multiply (reference form)
+uint16_t gf16_div_tab(uint16_t a, uint16_t b);
+
+// Maximum shard pointers a kernel takes by value.
+constexpr int kMaxShards = 34;
+
+}  // namespace gsec

@@ -1,0 +1,223 @@
+// layout.cu — moves between the KV tensors and shard rows.
+//
+// The reference packs K and V into a separate byte/word stream, pads it, and
+// then copies the stream into shard rows (benchmark/xor/main.py:80-93,
+// benchmark/rs/main.py:90-110, benchmark/rdp/kernel.cu:32-72) — three passes.
+// Here one kernel reads K and V where they lie and writes the rows:
+//   rows_pack   : stream = K ++ V (byte order), row r = stream[r*row_bytes ...],
+//                 zero past the stream end
+//   rows_unpack : the inverse
+//   bhtd_pack   : the reference RDP stream is token-major ([T, B*H*D] per
+//                 tensor, benchmark/rdp/main.py:66-67); this reads [B,H,T,D]
+//                 and applies the permutation on the fly
+//   bhtd_unpack : the inverse (benchmark/rdp/kernel.cu:305-345 + main.py:121-124)
+// Vector paths move 16 bytes per thread when every address involved is
+// 16-byte aligned; otherwise one byte (or u16 word) per thread.
+#include "common.cuh"
+#include "layout.cuh"
+
+namespace gsec {
+namespace {
+
+__device__ __forceinline__ uint4 ldv(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ void stv(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
+int grid_cap(int64_t items, int threads) {
+  int64_t g = (items + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (g > cap) g = cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+// ----------------------------------------------------------- rows <-> stream
+__global__ void rows_pack_vec(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
+                              int64_t pitch, int64_t row_bytes, int nrows) {
+  const int64_t vpr = row_bytes >> 4;  // row_bytes is a multiple of 16 here
+  const int64_t total = vpr * nrows;
+  const int64_t stream = len0 + len1;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = v / vpr, x = (v - r * vpr) << 4;
+    const int64_t i = r * row_bytes + x;
+    char* dst = rows + r * pitch + x;
+    if (i + 16 <= len0) {
+      stv(dst, ldv(s0 + i));
+    } else if (i >= len0 && i + 16 <= stream) {
+      stv(dst, ldv(s1 + (i - len0)));
+    } else if (i >= stream) {
+      stv(dst, vzero());
+    } else {
+      for (int b = 0; b < 16; ++b) {
+        const int64_t j = i + b;
+        dst[b] = j < len0 ? s0[j] : (j < stream ? s1[j - len0] : (char)0);
+      }
+    }
+  }
+}
+
+__global__ void rows_pack_byte(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
+                               int64_t pitch, int64_t row_bytes, int nrows) {
+  const int64_t total = row_bytes * nrows;
+  const int64_t stream = len0 + len1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / row_bytes, x = i - r * row_bytes;
+    rows[r * pitch + x] = i < len0 ? s0[i] : (i < stream ? s1[i - len0] : (char)0);
+  }
+}
+
+__global__ void rows_unpack_vec(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
+                                char* d1, int64_t len1) {
+  const int64_t stream = len0 + len1;
+  const int64_t total = (stream + 15) >> 4;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = v << 4;
+    const int64_t r = i / row_bytes, x = i - r * row_bytes;
+    const char* src = rows + r * pitch + x;
+    if (i + 16 <= len0) {
+      stv(d0 + i, ldv(src));
+    } else if (i >= len0 && i + 16 <= stream) {
+      stv(d1 + (i - len0), ldv(src));
+    } else {
+      for (int b = 0; b < 16 && i + b < stream; ++b) {
+        const int64_t j = i + b;
+        if (j < len0) d0[j] = src[b];
+        else d1[j - len0] = src[b];
+      }
+    }
+  }
+}
+
+__global__ void rows_unpack_byte(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
+                                 char* d1, int64_t len1) {
+  const int64_t stream = len0 + len1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < stream; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / row_bytes, x = i - r * row_bytes;
+    const char c = rows[r * pitch + x];
+    if (i < len0) d0[i] = c;
+    else d1[i - len0] = c;
+  }
+}
+
+// ------------------------------------------------------ [B,H,T,D] <-> rows --
+// Token-major stream index i (words): tensor = i / (T*n), j = i % (T*n),
+// t = j / n, c = j % n, bh = c / D, d = c % D; source word (bh*T + t)*D + d.
+struct Perm {
+  int64_t T, D, n, Tn;
+};
+
+__device__ __forceinline__ int64_t perm_src(const Perm& p, int64_t j) {
+  const int64_t t = j / p.n, c = j - t * p.n;
+  const int64_t bh = c / p.D, d = c - bh * p.D;
+  return (bh * p.T + t) * p.D + d;
+}
+
+// Vector path needs D % 8 == 0, S % 8 == 0, aligned rows/pitch/tensors: then a
+// group of 8 stream words maps to 8 consecutive source words.
+__global__ void bhtd_pack_kernel(const uint16_t* k, const uint16_t* v, Perm p, uint16_t* rows, int64_t pitch,
+                                 int64_t S, int nd, bool vec) {
+  const int64_t groups = (S + 7) >> 3;
+  const int64_t total = groups * nd;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = g / groups, c0 = (g - r * groups) << 3;
+    const int64_t i0 = r * S + c0;
+    uint16_t* dst = rows + r * pitch + c0;
+    if (vec && c0 + 8 <= S && i0 + 8 <= 2 * p.Tn) {
+      const uint16_t* src = i0 < p.Tn ? k + perm_src(p, i0) : v + perm_src(p, i0 - p.Tn);
+      stv(dst, ldv(src));
+    } else {
+      for (int b = 0; b < 8 && c0 + b < S; ++b) {
+        const int64_t i = i0 + b;
+        dst[b] = i < p.Tn ? k[perm_src(p, i)] : (i < 2 * p.Tn ? v[perm_src(p, i - p.Tn)] : (uint16_t)0);
+      }
+    }
+  }
+}
+
+__global__ void bhtd_unpack_kernel(const uint16_t* rows, int64_t pitch, int64_t S, Perm p, uint16_t* k,
+                                   uint16_t* v, bool vec) {
+  const int64_t total = (2 * p.Tn + 7) >> 3;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i0 = g << 3;
+    const int64_t r = i0 / S, c0 = i0 - r * S;
+    if (vec && c0 + 8 <= S && i0 + 8 <= 2 * p.Tn) {
+      const uint4 val = ldv(rows + r * pitch + c0);
+      uint16_t* dst = i0 < p.Tn ? k + perm_src(p, i0) : v + perm_src(p, i0 - p.Tn);
+      stv(dst, val);
+    } else {
+      for (int b = 0; b < 8 && i0 + b < 2 * p.Tn; ++b) {
+        const int64_t i = i0 + b;
+        const int64_t rr = i / S, cc = i - rr * S;
+        const uint16_t w = rows[rr * pitch + cc];
+        if (i < p.Tn) k[perm_src(p, i)] = w;
+        else v[perm_src(p, i - p.Tn)] = w;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int rows_pack(const void* s0, int64_t len0, const void* s1, int64_t len1, void* rows, int64_t pitch,
+              int64_t row_bytes, int nrows, cudaStream_t s) {
+  GSEC_REQUIRE(rows != nullptr && nrows >= 1 && row_bytes >= 1, "rows_pack: bad rows");
+  GSEC_REQUIRE(pitch >= row_bytes, "rows_pack: pitch < row_bytes");
+  GSEC_REQUIRE(len0 >= 0 && len1 >= 0 && (len0 == 0 || s0) && (len1 == 0 || s1), "rows_pack: bad stream");
+  GSEC_REQUIRE(len0 + len1 <= row_bytes * nrows, "rows_pack: stream longer than the rows");
+  const char* a = static_cast<const char*>(s0);
+  const char* b = static_cast<const char*>(s1);
+  const bool vec = (row_bytes % 16 == 0) && (pitch % 16 == 0) && (len0 % 16 == 0) && aligned16(rows) &&
+                   (len0 == 0 || aligned16(a)) && (len1 == 0 || aligned16(b));
+  const int threads = 256;
+  if (vec) {
+    rows_pack_vec<<<grid_cap((row_bytes >> 4) * nrows, threads), threads, 0, s>>>(
+        a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
+  } else {
+    rows_pack_byte<<<grid_cap(row_bytes * nrows, threads), threads, 0, s>>>(
+        a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
+  }
+  return check_launch("rows_pack");
+}
+
+int rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int nrows, void* d0, int64_t len0, void* d1,
+                int64_t len1, cudaStream_t s) {
+  GSEC_REQUIRE(rows != nullptr && nrows >= 1 && row_bytes >= 1, "rows_unpack: bad rows");
+  GSEC_REQUIRE(pitch >= row_bytes, "rows_unpack: pitch < row_bytes");
+  GSEC_REQUIRE(len0 >= 0 && len1 >= 0 && (len0 == 0 || d0) && (len1 == 0 || d1), "rows_unpack: bad outputs");
+  GSEC_REQUIRE(len0 + len1 <= row_bytes * nrows, "rows_unpack: stream longer than the rows");
+  char* a = static_cast<char*>(d0);
+  char* b = static_cast<char*>(d1);
+  const bool vec = (row_bytes % 16 == 0) && (pitch % 16 == 0) && (len0 % 16 == 0) && aligned16(rows) &&
+                   (len0 == 0 || aligned16(a)) && (len1 == 0 || aligned16(b));
+  const int threads = 256;
+  if (vec) {
+    rows_unpack_vec<<<grid_cap((len0 + len1 + 15) >> 4, threads), threads, 0, s>>>(
+        static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
+  } else {
+    rows_unpack_byte<<<grid_cap(len0 + len1, threads), threads, 0, s>>>(
+        static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
+  }
+  return check_launch("rows_unpack");
+}
+
+int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_t T, int64_t D, uint16_t* rows,
+              int64_t pitch, int nd, int64_t S, cudaStream_t s) {
+  GSEC_REQUIRE(k && v && rows && B >= 1 && H >= 1 && T >= 1 && D >= 1 && nd >= 1, "bhtd_pack: bad args");
+  Perm p{T, D, B * H * D, T * B * H * D};
+  GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_pack: rows too small");
+  const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
+  const int threads = 256;
+  bhtd_pack_kernel<<<grid_cap(((S + 7) >> 3) * nd, threads), threads, 0, s>>>(k, v, p, rows, pitch, S, nd, vec);
+  return check_launch("bhtd_pack_kernel");
+}
+
+int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t* k, uint16_t* v, int64_t B,
+                int64_t H, int64_t T, int64_t D, cudaStream_t s) {
+  GSEC_REQUIRE(k && v && rows && B >= 1 && H >= 1 && T >= 1 && D >= 1 && nd >= 1, "bhtd_unpack: bad args");
+  Perm p{T, D, B * H * D, T * B * H * D};
+  GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_unpack: rows too small");
+  const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
+  const int threads = 256;
+  bhtd_unpack_kernel<<<grid_cap((2 * p.Tn + 7) >> 3, threads), threads, 0, s>>>(rows, pitch, S, p, k, v, vec);
+  return check_launch("bhtd_unpack_kernel");
+}
+
+}  // namespace gsec

@@ -1,0 +1,18 @@
+// layout.cuh — KV tensors <-> shard rows (see layout.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace gsec {
+
+int rows_pack(const void* s0, int64_t len0, const void* s1, int64_t len1, void* rows, int64_t pitch,
+              int64_t row_bytes, int nrows, cudaStream_t s);
+int rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int nrows, void* d0, int64_t len0, void* d1,
+                int64_t len1, cudaStream_t s);
+// pitch and S in u16 words.
+int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_t T, int64_t D, uint16_t* rows,
+              int64_t pitch, int nd, int64_t S, cudaStream_t s);
+int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t* k, uint16_t* v, int64_t B,
+                int64_t H, int64_t T, int64_t D, cudaStream_t s);
+
+}  // namespace gsec

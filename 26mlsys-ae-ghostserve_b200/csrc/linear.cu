@@ -1,0 +1,352 @@
+// linear.cu — kernels for position-wise linear codes (XOR, GF(2^8), GF(2^16)).
+//
+// Layout assumed by the vector kernels: every shard pointer 16-byte aligned and
+// `split`/`begin` multiples of 16, so each thread moves whole 16-byte vectors
+// that never straddle a segment boundary.  Anything else goes to the scalar
+// kernel (same arithmetic, one symbol per thread).
+//
+// GF constant multiplication uses a 256-entry table per input shard in shared
+// memory.  Entry x of input i packs the products coef[j][i]*x of all outputs j
+// (one byte each for GF(2^8), one u16 for GF(2^16) split into low/high byte
+// tables), so one shared-memory load serves every parity shard.  Each table is
+// replicated R times and lane l reads copy l % R: with R = 32 the 32 lanes of a
+// warp always hit 32 different banks whatever the data bytes are.
+#include "linear.cuh"
+
+namespace gsec {
+namespace {
+
+__device__ __forceinline__ const char* seg(const char* lo, const char* hi, int64_t split,
+                                           int64_t x) {
+  return x < split ? lo + x : hi + (x - split);
+}
+__device__ __forceinline__ char* seg(char* lo, char* hi, int64_t split, int64_t x) {
+  return x < split ? lo + x : hi + (x - split);
+}
+
+// Plain (coherent) 16-byte load with no L1 allocation: shards are streamed once,
+// and the pointer may be a peer GPU's memory mapped over NVLink.
+__device__ __forceinline__ uint4 ld16(const char* p) {
+  uint4 v;
+  asm("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st16(char* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// Sub-vector tail [t0, end) of every output, one thread, symbol at a time.
+__device__ void linear_tail(const LinearPass& a, int64_t t0) {
+  if (a.field == Field::GF16) {
+    for (int64_t x = t0; x + 2 <= a.end; x += 2) {
+      for (int j = 0; j < a.nout; ++j) {
+        uint32_t acc = 0;
+        for (int i = 0; i < a.nin; ++i) {
+          const uint16_t w = *reinterpret_cast<const uint16_t*>(seg(a.in_lo[i], a.in_hi[i], a.split, x));
+          acc ^= gf16_mul(w, a.coef[j][i]);
+        }
+        if (x < a.out_end[j])
+          *reinterpret_cast<uint16_t*>(seg(a.out_lo[j], a.out_hi[j], a.split, x)) = (uint16_t)acc;
+      }
+    }
+    return;
+  }
+  for (int64_t x = t0; x < a.end; ++x) {
+    for (int j = 0; j < a.nout; ++j) {
+      uint32_t acc = 0;
+      for (int i = 0; i < a.nin; ++i) {
+        const uint8_t b = *reinterpret_cast<const uint8_t*>(seg(a.in_lo[i], a.in_hi[i], a.split, x));
+        acc ^= (a.field == Field::XOR) ? b : gf8_mul(b, a.coef[j][i] & 0xffu);
+      }
+      if (x < a.out_end[j]) *reinterpret_cast<uint8_t*>(seg(a.out_lo[j], a.out_hi[j], a.split, x)) = (uint8_t)acc;
+    }
+  }
+}
+
+// ----------------------------------------------------------------- XOR ------
+// every output = XOR of all inputs (extra outputs receive copies).  VPT independent 16-byte vectors per thread
+// per step keep nin*VPT loads in flight.
+template <int VPT>
+__global__ void __launch_bounds__(256) xor_vec_kernel(const LinearPass a) {
+  const int64_t nvec = (a.end - a.begin) >> 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * VPT;
+  for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x * VPT + threadIdx.x; v0 < nvec; v0 += step) {
+    uint4 acc[VPT];
+    int64_t off[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      acc[j] = vzero();
+      off[j] = a.begin + ((v0 + (int64_t)j * blockDim.x) << 4);
+    }
+#pragma unroll 4
+    for (int i = 0; i < a.nin; ++i) {
+      const char* lo = a.in_lo[i];
+      const char* hi = a.in_hi[i];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        if (v0 + (int64_t)j * blockDim.x < nvec) acc[j] = vxor(acc[j], ld16(seg(lo, hi, a.split, off[j])));
+    }
+    for (int o = 0; o < a.nout; ++o) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        if (v0 + (int64_t)j * blockDim.x < nvec && off[j] + 16 <= a.out_end[o])
+          st16(seg(a.out_lo[o], a.out_hi[o], a.split, off[j]), acc[j]);
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
+}
+
+// --------------------------------------------------------------- GF(2^8) ----
+template <int NOUT, int R>
+__global__ void __launch_bounds__(1024) gf8_vec_kernel(const LinearPass a) {
+  extern __shared__ uint32_t tab[];  // [nin][256][R]
+  for (int e = threadIdx.x; e < a.nin * 256; e += blockDim.x) {
+    const int i = e >> 8, x = e & 255;
+    uint32_t entry = 0;
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j) entry |= gf8_mul((uint32_t)(a.coef[j][i] & 0xffu), (uint32_t)x) << (8 * j);
+    uint32_t* dst = tab + (size_t)e * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) dst[r] = entry;
+  }
+  __syncthreads();
+  const uint32_t* tl = tab + (threadIdx.x & (R - 1));
+
+  const int64_t nvec = (a.end - a.begin) >> 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
+    const int64_t off = a.begin + (v << 4);
+    uint32_t o[NOUT][4];
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0u;
+#pragma unroll 2
+    for (int i = 0; i < a.nin; ++i) {
+      const uint4 xv = ld16(seg(a.in_lo[i], a.in_hi[i], a.split, off));
+      const uint32_t* t = tl + (size_t)i * 256 * R;
+      const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t x = xs[w];
+        const uint32_t t0 = t[(x & 0xffu) * R];
+        const uint32_t t1 = t[((x >> 8) & 0xffu) * R];
+        const uint32_t t2 = t[((x >> 16) & 0xffu) * R];
+        const uint32_t t3 = t[(x >> 24) * R];
+        // 4x4 byte transpose: output j gets byte j of t0..t3 (the products of data bytes 0..3).
+        const uint32_t u = __byte_perm(t0, t1, 0x5140);
+        const uint32_t q = __byte_perm(t2, t3, 0x5140);
+        o[0][w] ^= __byte_perm(u, q, 0x5410);
+        if (NOUT > 1) o[NOUT > 1 ? 1 : 0][w] ^= __byte_perm(u, q, 0x7632);
+        if (NOUT > 2) {
+          const uint32_t u2 = __byte_perm(t0, t1, 0x7362);
+          const uint32_t q2 = __byte_perm(t2, t3, 0x7362);
+          o[NOUT > 2 ? 2 : 0][w] ^= __byte_perm(u2, q2, 0x5410);
+          if (NOUT > 3) o[NOUT > 3 ? 3 : 0][w] ^= __byte_perm(u2, q2, 0x7632);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j)
+      if (off + 16 <= a.out_end[j])
+        st16(seg(a.out_lo[j], a.out_hi[j], a.split, off), make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
+}
+
+// -------------------------------------------------------------- GF(2^16) ----
+// Constant multiply c*w = c*(w & 0xff) ^ c*(w & 0xff00): two byte tables per
+// input, entries pack the u16 products of outputs 0 (low half) and 1 (high).
+template <int NOUT, int R>
+__global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
+  extern __shared__ uint32_t tab[];  // [nin][2][256][R]
+  for (int e = threadIdx.x; e < a.nin * 512; e += blockDim.x) {
+    const int i = e >> 9, h = (e >> 8) & 1, x = e & 255;
+    const uint32_t v = h ? ((uint32_t)x << 8) : (uint32_t)x;
+    uint32_t entry = gf16_mul(v, a.coef[0][i]);
+    if (NOUT > 1) entry |= gf16_mul(v, a.coef[NOUT > 1 ? 1 : 0][i]) << 16;
+    uint32_t* dst = tab + (size_t)e * R;
+#pragma unroll
+    for (int r = 0; r < R; ++r) dst[r] = entry;
+  }
+  __syncthreads();
+  const uint32_t* tl = tab + (threadIdx.x & (R - 1));
+
+  const int64_t nvec = (a.end - a.begin) >> 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
+    const int64_t off = a.begin + (v << 4);
+    uint32_t o[NOUT][4];
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0u;
+#pragma unroll 2
+    for (int i = 0; i < a.nin; ++i) {
+      const uint4 xv = ld16(seg(a.in_lo[i], a.in_hi[i], a.split, off));
+      const uint32_t* tlo = tl + (size_t)i * 512 * R;
+      const uint32_t* thi = tlo + 256 * R;
+      const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t x = xs[w];
+        const uint32_t p0 = tlo[(x & 0xffu) * R] ^ thi[((x >> 8) & 0xffu) * R];
+        const uint32_t p1 = tlo[((x >> 16) & 0xffu) * R] ^ thi[(x >> 24) * R];
+        o[0][w] ^= __byte_perm(p0, p1, 0x5410);
+        if (NOUT > 1) o[NOUT > 1 ? 1 : 0][w] ^= __byte_perm(p0, p1, 0x7632);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j)
+      if (off + 16 <= a.out_end[j])
+        st16(seg(a.out_lo[j], a.out_hi[j], a.split, off), make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
+}
+
+// ---------------------------------------------------------------- scalar ----
+// Misaligned layouts: one byte (XOR/GF8) or one u16 word (GF16) per thread.
+__global__ void __launch_bounds__(256) linear_scalar_kernel(const LinearPass a) {
+  const int sym = (a.field == Field::GF16) ? 2 : 1;
+  const int64_t nsym = (a.end - a.begin) / sym;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; s < nsym; s += step) {
+    const int64_t x = a.begin + s * sym;
+    for (int j = 0; j < a.nout; ++j) {
+      uint32_t acc = 0;
+      for (int i = 0; i < a.nin; ++i) {
+        const char* p = seg(a.in_lo[i], a.in_hi[i], a.split, x);
+        if (a.field == Field::GF16) acc ^= gf16_mul(*reinterpret_cast<const uint16_t*>(p), a.coef[j][i]);
+        else if (a.field == Field::GF8) acc ^= gf8_mul(*reinterpret_cast<const uint8_t*>(p), a.coef[j][i] & 0xffu);
+        else acc ^= *reinterpret_cast<const uint8_t*>(p);
+      }
+      if (x + sym <= a.out_end[j]) {
+        char* q = seg(a.out_lo[j], a.out_hi[j], a.split, x);
+        if (a.field == Field::GF16) *reinterpret_cast<uint16_t*>(q) = (uint16_t)acc;
+        else *reinterpret_cast<uint8_t*>(q) = (uint8_t)acc;
+      }
+    }
+  }
+}
+
+bool pass_aligned(const LinearPass& a) {
+  if ((a.begin & 15) || (a.split & 15)) return false;
+  for (int i = 0; i < a.nin; ++i)
+    if (!aligned16(a.in_lo[i]) || !aligned16(a.in_hi[i])) return false;
+  for (int j = 0; j < a.nout; ++j)
+    if (!aligned16(a.out_lo[j]) || !aligned16(a.out_hi[j])) return false;
+  return true;
+}
+
+template <typename K>
+int occupancy_grid(K kernel, int threads, size_t smem, int64_t work_items) {
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  if (per_sm < 1) per_sm = 1;
+  int64_t grid = (int64_t)sm_count() * per_sm;
+  const int64_t need = (work_items + threads - 1) / threads;
+  if (need < grid) grid = need;
+  return (int)(grid < 1 ? 1 : grid);
+}
+
+// Largest replication R (power of two <= 32) whose tables fit in `budget` bytes.
+int pick_replicas(int64_t bytes_per_copy, int64_t budget) {
+  int r = 32;
+  while (r > 1 && bytes_per_copy * r > budget) r >>= 1;
+  return r;
+}
+
+template <int NOUT, int R>
+int launch_gf8(const LinearPass& a, cudaStream_t s) {
+  const size_t smem = (size_t)a.nin * 256 * 4 * R;
+  auto k = gf8_vec_kernel<NOUT, R>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return check_launch("gf8 smem attribute");
+  const int threads = 1024;
+  const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
+  k<<<grid, threads, smem, s>>>(a);
+  return check_launch("gf8_vec_kernel");
+}
+
+template <int NOUT, int R>
+int launch_gf16(const LinearPass& a, cudaStream_t s) {
+  const size_t smem = (size_t)a.nin * 512 * 4 * R;
+  auto k = gf16_vec_kernel<NOUT, R>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return check_launch("gf16 smem attribute");
+  const int threads = 1024;
+  const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
+  k<<<grid, threads, smem, s>>>(a);
+  return check_launch("gf16_vec_kernel");
+}
+
+template <int NOUT>
+int dispatch_gf8(const LinearPass& a, int r, cudaStream_t s) {
+  switch (r) {
+    case 32: return launch_gf8<NOUT, 32>(a, s);
+    case 16: return launch_gf8<NOUT, 16>(a, s);
+    case 8: return launch_gf8<NOUT, 8>(a, s);
+    case 4: return launch_gf8<NOUT, 4>(a, s);
+    case 2: return launch_gf8<NOUT, 2>(a, s);
+    default: return launch_gf8<NOUT, 1>(a, s);
+  }
+}
+template <int NOUT>
+int dispatch_gf16(const LinearPass& a, int r, cudaStream_t s) {
+  switch (r) {
+    case 32: return launch_gf16<NOUT, 32>(a, s);
+    case 16: return launch_gf16<NOUT, 16>(a, s);
+    case 8: return launch_gf16<NOUT, 8>(a, s);
+    case 4: return launch_gf16<NOUT, 4>(a, s);
+    case 2: return launch_gf16<NOUT, 2>(a, s);
+    default: return launch_gf16<NOUT, 1>(a, s);
+  }
+}
+
+constexpr int64_t kTableBudget = 192 * 1024;
+
+}  // namespace
+
+int run_linear(const LinearPass& a, cudaStream_t s) {
+  if (a.end <= a.begin || a.nout == 0) return GSEC_OK;
+  if (a.nin < 1 || a.nin > kLinMaxIn || a.nout < 0 || a.nout > kLinMaxOut) {
+    set_error("linear pass: nin=%d nout=%d out of range", a.nin, a.nout);
+    return GSEC_EINVAL;
+  }
+  if (!pass_aligned(a)) {
+    const int threads = 256;
+    const int64_t nsym = (a.end - a.begin) / (a.field == Field::GF16 ? 2 : 1);
+    const int grid = occupancy_grid(linear_scalar_kernel, threads, 0, nsym);
+    linear_scalar_kernel<<<grid, threads, 0, s>>>(a);
+    return check_launch("linear_scalar_kernel");
+  }
+  switch (a.field) {
+    case Field::XOR: {
+      constexpr int VPT = 4;
+      const int threads = 256;
+      const int grid = occupancy_grid(xor_vec_kernel<VPT>, threads, 0, ((a.end - a.begin) >> 4) / VPT + 1);
+      xor_vec_kernel<VPT><<<grid, threads, 0, s>>>(a);
+      return check_launch("xor_vec_kernel");
+    }
+    case Field::GF8: {
+      const int r = pick_replicas((int64_t)a.nin * 256 * 4, kTableBudget);
+      switch (a.nout) {
+        case 1: return dispatch_gf8<1>(a, r, s);
+        case 2: return dispatch_gf8<2>(a, r, s);
+        case 3: return dispatch_gf8<3>(a, r, s);
+        default: return dispatch_gf8<4>(a, r, s);
+      }
+    }
+    case Field::GF16: {
+      if (a.nout > 2) {
+        set_error("GF16 pass has at most two outputs");
+        return GSEC_EINVAL;
+      }
+      const int r = pick_replicas((int64_t)a.nin * 512 * 4, kTableBudget);
+      return a.nout == 1 ? dispatch_gf16<1>(a, r, s) : dispatch_gf16<2>(a, r, s);
+    }
+  }
+  return GSEC_EINVAL;
+}
+
+}  // namespace gsec

@@ -1,0 +1,247 @@
+// rdp.cu — Row-Diagonal Parity (Corbett et al., "Row-Diagonal Parity for Double
+// Disk Failure Correction", FAST 2004) over KV shards.
+//
+// Geometry (p prime, k <= p-1 data shards): every shard is cut into stripes of
+// (p-1) units of `unit` bytes.  In a stripe, cell (r, c) is unit r of column c,
+// r in [0, p-2]; columns 0..p-2 are data (columns k..p-2 are virtual all-zero
+// shards, i.e. the shortened code), column p-1 is the row parity P and column p
+// the diagonal parity Q.
+//   P[r]  = XOR_{c=0}^{p-2} D[r][c]
+//   cell (r, c) for c in [0, p-1] lies on diagonal (r + c) mod p;
+//   Q[d]  = XOR of the cells of diagonal d, d in [0, p-2] (diagonal p-1 is not stored).
+// Diagonal arithmetic is per unit, so a thread owning byte lane b of a stripe
+// XORs whole 16-byte vectors of cells; with p a template parameter every
+// (r + c) mod p is a compile-time register index.
+//
+// Decode of up to two erased columns: one pass over the surviving cells of a
+// stripe accumulates row syndromes R[r] (XOR over surviving columns 0..p-1) and
+// diagonal syndromes S[d] (same over diagonal d, plus Q[d] if Q survives).
+// Each erased cell is a fixed XOR of syndromes that depends only on which
+// columns are erased; the host solves that GF(2) system once per call and passes
+// one bit mask per erased cell.
+#include <vector>
+
+#include "common.cuh"
+#include "rdp.cuh"
+
+namespace gsec {
+namespace {
+
+__device__ __forceinline__ const char* seg(const char* lo, const char* hi, int64_t split, int64_t x) {
+  return x < split ? lo + x : hi + (x - split);
+}
+__device__ __forceinline__ char* seg(char* lo, char* hi, int64_t split, int64_t x) {
+  return x < split ? lo + x : hi + (x - split);
+}
+__device__ __forceinline__ uint4 ld16(const char* p) {
+  uint4 v;
+  asm("ld.global.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st16(char* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- encode ----
+template <int P>
+__global__ void __launch_bounds__(256) rdp_encode_kernel(const RdpEncodeArgs a) {
+  const int64_t lanes = a.unit >> 4;
+  const int64_t stripe_bytes = (int64_t)(P - 1) * a.unit;
+  const int64_t items = (a.s_end - a.s_begin) * lanes;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < items; g += step) {
+    const int64_t stripe = a.s_begin + g / lanes;
+    const int64_t lane = g - (stripe - a.s_begin) * lanes;
+    const int64_t base = stripe * stripe_bytes + (lane << 4);
+    const bool full = (stripe + 1) * stripe_bytes <= a.data_bytes;
+    uint4 q[P];
+#pragma unroll
+    for (int d = 0; d < P; ++d) q[d] = vzero();
+#pragma unroll
+    for (int r = 0; r < P - 1; ++r) {
+      const int64_t off = base + (int64_t)r * a.unit;
+      uint4 x[P - 1];
+#pragma unroll
+      for (int c = 0; c < P - 1; ++c) {
+        x[c] = vzero();
+        if (c < a.k && (full || off < a.data_bytes)) x[c] = ld16(seg(a.d_lo[c], a.d_hi[c], a.split, off));
+      }
+      uint4 prow = vzero();
+#pragma unroll
+      for (int c = 0; c < P - 1; ++c) {
+        prow = vxor(prow, x[c]);
+        if ((r + c) % P != P - 1) q[(r + c) % P] = vxor(q[(r + c) % P], x[c]);
+      }
+      st16(a.parity[0] + off, prow);
+      if ((r + P - 1) % P != P - 1) q[(r + P - 1) % P] = vxor(q[(r + P - 1) % P], prow);
+    }
+#pragma unroll
+    for (int d = 0; d < P - 1; ++d) st16(a.parity[1] + base + (int64_t)d * a.unit, q[d]);
+  }
+}
+
+// ---------------------------------------------------------------- decode ----
+template <int P>
+__global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) {
+  constexpr int NS = 2 * (P - 1);
+  const int64_t lanes = a.unit >> 4;
+  const int64_t stripe_bytes = (int64_t)(P - 1) * a.unit;
+  const int64_t items = (a.s_end - a.s_begin) * lanes;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < items; g += step) {
+    const int64_t stripe = a.s_begin + g / lanes;
+    const int64_t lane = g - (stripe - a.s_begin) * lanes;
+    const int64_t base = stripe * stripe_bytes + (lane << 4);
+    const bool full = (stripe + 1) * stripe_bytes <= a.data_bytes;
+    uint4 syn[NS];  // [0, P-1): row syndromes R[r]; [P-1, NS): diagonal syndromes S[d]
+#pragma unroll
+    for (int j = 0; j < NS; ++j) syn[j] = vzero();
+#pragma unroll
+    for (int c = 0; c <= P; ++c) {
+      if (!((a.alive >> c) & 1u)) continue;
+      const bool is_data = c < P - 1;
+#pragma unroll
+      for (int r = 0; r < P - 1; ++r) {
+        const int64_t off = base + (int64_t)r * a.unit;
+        if (is_data && !(full || off < a.data_bytes)) continue;
+        const uint4 v = ld16(seg(a.lo[c], a.hi[c], a.split, off));
+        if (c <= P - 1) {
+          syn[r] = vxor(syn[r], v);
+          if ((r + c) % P != P - 1) syn[(P - 1) + (r + c) % P] = vxor(syn[(P - 1) + (r + c) % P], v);
+        } else {
+          syn[(P - 1) + r] = vxor(syn[(P - 1) + r], v);
+        }
+      }
+    }
+    for (int e = 0; e < a.nout; ++e) {
+      const bool out_data = a.out_col[e] < P - 1;
+#pragma unroll
+      for (int r = 0; r < P - 1; ++r) {
+        const int64_t off = base + (int64_t)r * a.unit;
+        const uint32_t m = a.mask[e][r];
+        uint4 o = vzero();
+#pragma unroll
+        for (int j = 0; j < NS; ++j)
+          if ((m >> j) & 1u) o = vxor(o, syn[j]);
+        if (!out_data || off < a.data_bytes) st16(seg(a.out_lo[e], a.out_hi[e], a.split, off), o);
+      }
+    }
+  }
+}
+
+template <typename K>
+int grid_for(K kernel, int threads, int64_t items) {
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+  if (per_sm < 1) per_sm = 1;
+  int64_t grid = (int64_t)sm_count() * per_sm;
+  const int64_t need = (items + threads - 1) / threads;
+  if (need < grid) grid = need;
+  return (int)(grid < 1 ? 1 : grid);
+}
+
+template <int P>
+int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
+  const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
+  const int threads = 256;
+  const int grid = grid_for(rdp_encode_kernel<P>, threads, items);
+  rdp_encode_kernel<P><<<grid, threads, 0, s>>>(a);
+  return check_launch("rdp_encode_kernel");
+}
+template <int P>
+int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
+  const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
+  const int threads = 256;
+  const int grid = grid_for(rdp_decode_kernel<P>, threads, items);
+  rdp_decode_kernel<P><<<grid, threads, 0, s>>>(a);
+  return check_launch("rdp_decode_kernel");
+}
+
+}  // namespace
+
+bool rdp_prime_supported(int p) {
+  return p == 3 || p == 5 || p == 7 || p == 11 || p == 13 || p == 17;
+}
+
+int rdp_encode(const RdpEncodeArgs& a, cudaStream_t s) {
+  if (a.s_end <= a.s_begin) return GSEC_OK;
+  switch (a.p) {
+    case 3: return launch_encode<3>(a, s);
+    case 5: return launch_encode<5>(a, s);
+    case 7: return launch_encode<7>(a, s);
+    case 11: return launch_encode<11>(a, s);
+    case 13: return launch_encode<13>(a, s);
+    case 17: return launch_encode<17>(a, s);
+    default: set_error("RDP prime p=%d not supported (3,5,7,11,13,17)", a.p); return GSEC_EUNSUPPORTED;
+  }
+}
+
+int rdp_decode(const RdpDecodeArgs& a, cudaStream_t s) {
+  if (a.s_end <= a.s_begin || a.nout == 0) return GSEC_OK;
+  switch (a.p) {
+    case 3: return launch_decode<3>(a, s);
+    case 5: return launch_decode<5>(a, s);
+    case 7: return launch_decode<7>(a, s);
+    case 11: return launch_decode<11>(a, s);
+    case 13: return launch_decode<13>(a, s);
+    case 17: return launch_decode<17>(a, s);
+    default: set_error("RDP prime p=%d not supported (3,5,7,11,13,17)", a.p); return GSEC_EUNSUPPORTED;
+  }
+}
+
+// Solve the erased cells of one stripe as XORs of syndromes.
+//   cols: erased columns in [0, p] (p-1 = row parity, p = diagonal parity).
+// Unknown u = e*(p-1) + r is cell (r, cols[e]).  Syndrome ids: r for R[r],
+// (p-1)+d for S[d].  Equations (over GF(2)):
+//   row r      : XOR_{e: cols[e] <= p-1} x(e, r)                           = R[r]
+//   diagonal d : XOR_{e: cols[e] <= p-1, r=(d-cols[e]) mod p, r<p-1} x(e, r)
+//                ^ [Q erased] x(Q, d)                                       = S[d]
+int rdp_solve_masks(int p, const int* cols, int ncols, uint32_t mask[2][16]) {
+  const int rows = p - 1;
+  const int nunk = ncols * rows;
+  const int neq = 2 * rows;
+  std::vector<uint64_t> lhs(neq, 0);
+  std::vector<uint32_t> rhs(neq, 0);
+  for (int r = 0; r < rows; ++r) {
+    rhs[r] = 1u << r;
+    for (int e = 0; e < ncols; ++e)
+      if (cols[e] <= p - 1) lhs[r] |= 1ull << (e * rows + r);
+  }
+  for (int d = 0; d < rows; ++d) {
+    const int q = rows + d;
+    rhs[q] = 1u << q;
+    for (int e = 0; e < ncols; ++e) {
+      if (cols[e] <= p - 1) {
+        const int r = ((d - cols[e]) % p + p) % p;
+        if (r < rows) lhs[q] |= 1ull << (e * rows + r);
+      } else {
+        lhs[q] |= 1ull << (e * rows + d);
+      }
+    }
+  }
+  // Gauss-Jordan over GF(2): pivot on each unknown in turn.
+  std::vector<int> pivot_of(nunk, -1);
+  std::vector<bool> used(neq, false);
+  for (int u = 0; u < nunk; ++u) {
+    int piv = -1;
+    for (int i = 0; i < neq; ++i)
+      if (!used[i] && ((lhs[i] >> u) & 1ull)) { piv = i; break; }
+    if (piv < 0) {
+      set_error("RDP erasure pattern is not decodable (singular system)");
+      return GSEC_EUNRECOVERABLE;
+    }
+    used[piv] = true;
+    pivot_of[u] = piv;
+    for (int i = 0; i < neq; ++i)
+      if (i != piv && ((lhs[i] >> u) & 1ull)) { lhs[i] ^= lhs[piv]; rhs[i] ^= rhs[piv]; }
+  }
+  for (int e = 0; e < ncols; ++e)
+    for (int r = 0; r < rows; ++r) mask[e][r] = rhs[pivot_of[e * rows + r]];
+  return GSEC_OK;
+}
+
+}  // namespace gsec

@@ -1,0 +1,43 @@
+// rdp.cuh — textbook Row-Diagonal Parity kernels (see rdp.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace gsec {
+
+constexpr int kRdpMaxCols = 18;  // p + 1 columns for p <= 17
+
+struct RdpEncodeArgs {
+  const char* d_lo[16];
+  const char* d_hi[16];
+  char* parity[2];      // P and Q shard bases
+  int64_t split;
+  int64_t data_bytes;   // data shard bytes; reads at or past this offset are zero
+  int64_t unit;         // stripe unit bytes (multiple of 16)
+  int64_t s_begin, s_end;  // stripe range
+  int k;
+  int p;
+};
+
+struct RdpDecodeArgs {
+  const char* lo[kRdpMaxCols];  // indexed by column: 0..p-2 data, p-1 = P, p = Q
+  const char* hi[kRdpMaxCols];
+  char* out_lo[2];
+  char* out_hi[2];
+  uint32_t mask[2][16];  // per erased column and row: syndromes to XOR
+  int out_col[2];
+  int nout;
+  uint32_t alive;        // bit c set: column c is read
+  int64_t split;
+  int64_t data_bytes;
+  int64_t unit;
+  int64_t s_begin, s_end;
+  int p;
+};
+
+bool rdp_prime_supported(int p);
+int rdp_encode(const RdpEncodeArgs& a, cudaStream_t s);
+int rdp_decode(const RdpDecodeArgs& a, cudaStream_t s);
+int rdp_solve_masks(int p, const int* cols, int ncols, uint32_t mask[2][16]);
+
+}  // namespace gsec

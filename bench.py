@@ -1,0 +1,383 @@
+#!/usr/bin/env python3
+"""bench.py — KV parity encode throughput of the B200 erasure-coding engine.
+
+Default workload: textbook RDP with p=7 over 6 data shards
++ row parity P + diagonal parity Q, 4 KiB stripe units; each data shard is one
+rank's KV for one 2048-token chunk of a Llama-3.1-8B-architecture model at
+TP=8 (K and V [32 layers, 2048 tokens, 1 kv-head, 128] bf16 ~ N(0,1), seeded):
+32 MiB, padded to 1366 stripes in the parity shards.
+
+A step = one encode of that codeword.  ``value`` is algorithmic bytes
+((k+m) shards: k*32 MiB read + 2 parity shards written) / device time, summed
+over ranks.  ``e2e`` runs the same step through the host pipeline (pinned host
+shards -> H2D -> encode -> D2H parity), copies inside the timed region.
+
+N GPUs (torchrun): each rank owns one codeword whose six data shards live on
+six different GPUs (shard j of rank c's codeword on GPU (c + j) mod N, j = 0
+local).  Every rank maps its peers' shard buffers over CUDA IPC and its encode
+kernel reads them with NVLink peer loads — the gather of the reference hook
+fused into the encode.  Per-GPU work is fixed (weak scaling).
+
+``--impl reference`` times the reference path's CPU port (the C/OpenMP oracle
+of the same code) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "26mlsys-ae-ghostserve_b200"
+METRIC = "KV parity encode GB/s/GPU (% HBM/NVLink roof); prefill tok/s overhead"
+MIB = 1 << 20
+
+WORKLOADS = {
+    "rdp_p7": dict(scheme="rdp", k=6, m=2, p=7, unit=4096, shard=32 * MIB, kv="bf16",
+                   desc="config 1: textbook RDP p=7, 6 data + P + Q, 4 KiB units, 32 MiB bf16 KV shard per rank"),
+    "rs8_6_2": dict(scheme="rs8", k=6, m=2, p=0, unit=0, shard=16 * MIB, kv="fp8",
+                    desc="config 2: RS(6,2) GF(2^8)/0x11d Cauchy, 16 MiB fp8 (uniform bytes) KV shard per rank"),
+    "xor_7": dict(scheme="xor", k=7, m=1, p=0, unit=0, shard=32 * MIB, kv="bf16",
+                  desc="config 0: XOR 7+1, 32 MiB bf16 KV shard per rank"),
+}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profiles(kernel_tag: str):
+    """Per-launch DRAM bytes recorded by an ncu capture summary under profiles/."""
+    path = os.path.join(ROOT, "profiles", kernel_tag + ".md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed loop runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def kv_shards(torch, wl, seed: int, count: int, device):
+    """Seeded synthetic KV shards on the device (bf16 N(0,1) or fp8 uniform bytes)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _ in range(count):
+        if wl["kv"] == "bf16":
+            x = torch.randn(wl["shard"] // 2, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+            out.append(x.view(torch.uint8))
+        else:
+            out.append(torch.randint(0, 256, (wl["shard"],), generator=gen, device=device, dtype=torch.uint8))
+    return out
+
+
+# --------------------------------------------------------------- reference ----
+def cpu_encode_rate(wl, host_data, seconds: float, max_reps=None):
+    """C/OpenMP oracle encode of the workload on the host cores: (GB/s, reps, threads, sample)."""
+    import numpy as np
+
+    from oracle import cpu
+
+    threads = len(os.sched_getaffinity(0))
+    k, m = wl["k"], wl["m"]
+    nbytes = host_data[0].size
+    if wl["scheme"] == "rdp":
+        sb = (wl["p"] - 1) * wl["unit"]
+        pb = -(-nbytes // sb) * sb
+        out = (np.empty(pb, np.uint8), np.empty(pb, np.uint8))
+
+        def run():
+            cpu.rdp_encode(host_data, wl["p"], wl["unit"], threads=threads, out=out)
+    elif wl["scheme"] == "rs8":
+        pb = nbytes
+        out = [np.empty(nbytes, np.uint8) for _ in range(m)]
+
+        def run():
+            cpu.rs8_encode(host_data, m, threads=threads, out=out)
+    else:
+        pb = nbytes
+
+        def run():
+            cpu.xor_encode(host_data, threads=threads)
+    run()  # warm: page-in and thread pool
+    alg = k * nbytes + m * pb
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_reps is not None and reps >= max_reps):
+            break
+    return alg * reps / el / 1e9, reps, threads, el
+
+
+def sample_host_data(wl, frac: float = 1.0):
+    import numpy as np
+
+    rng = np.random.default_rng(1)
+    n = wl["shard"]
+    if frac < 1.0:
+        g = (wl["p"] - 1) * wl["unit"] if wl["scheme"] == "rdp" else 4096
+        n = max(g, int(n * frac) // g * g)
+    if wl["kv"] == "bf16":
+        out = []
+        for _ in range(wl["k"]):
+            x = rng.standard_normal(n // 2, dtype=np.float32)
+            out.append((x.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8))
+        return out
+    return [rng.integers(0, 256, n, dtype=np.uint8) for _ in range(wl["k"])]
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    data = sample_host_data(wl)
+    _, _, threads, t1 = cpu_encode_rate(wl, data, 0.0, max_reps=1)
+    # each step: a bounded sample of the workload so the whole run stays within ~2 minutes
+    budget = 90.0
+    frac = min(1.0, budget / max(1e-9, (args.steps + args.warmup) * t1))
+    if frac < 1.0:
+        data = sample_host_data(wl, frac)
+    nbytes = data[0].size
+    for _ in range(args.warmup):
+        cpu_encode_rate(wl, data, 0.0, max_reps=1)
+    rate, reps, threads, el = cpu_encode_rate(wl, data, 0.0, max_reps=args.steps)
+    sample = f"{wl['k']} x {nbytes} B shards per step ({nbytes / wl['shard']:.3f} of the workload), {reps} steps"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(rate, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * el / max(1, reps), 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": wl["desc"]},
+        "cpu_baseline": {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(rate, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference has no CPU encoder; this is the C/OpenMP port of the same code (oracle/cpu)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours ----
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    g = importlib.import_module(PKG)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    spec = g.CodeSpec(wl["scheme"], wl["k"], wl["m"], wl["p"], wl["unit"])
+    k, m = spec.k, spec.m
+    nbytes = wl["shard"]
+    pbytes = spec.parity_bytes(nbytes)
+    alg_bytes = k * nbytes + m * pbytes
+
+    # My data buffer holds k shard slots; slot j is shard j of codeword (rank - j) mod world.
+    slots = kv_shards(torch, wl, seed=100 + rank, count=k, device=device)
+    parity = [torch.empty(pbytes, dtype=torch.uint8, device=device) for _ in range(m)]
+    peer_group = None
+    remote_bytes = 0
+    if world > 1:
+        p2p = importlib.import_module(PKG + ".p2p")
+        peer_group = p2p.PeerGroup.create(slots)  # maps every rank's k slots
+        data_ptrs = [peer_group.ptr((rank + j) % world, j) for j in range(k)]
+        remote_bytes = sum(nbytes for j in range(k) if (rank + j) % world != rank)
+    else:
+        data_ptrs = [t.data_ptr() for t in slots]
+    par_ptrs = [t.data_ptr() for t in parity]
+    stream = torch.cuda.current_stream()
+    sh = int(stream.cuda_stream)
+
+    def step():
+        g.codec.encode_ptrs(spec, data_ptrs, None, nbytes, nbytes, par_ptrs, 0, pbytes, sh)
+
+    def barrier():
+        if world > 1:
+            t = torch.ones(1, device=device)
+            dist.all_reduce(t)  # stream-ordered: peers' buffers are written before anyone reads them
+            torch.cuda.synchronize()
+
+    barrier()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(local).start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    barrier()
+    ms_step = ms / args.steps
+    per_gpu = alg_bytes / (ms_step * 1e-3) / 1e9
+    value = per_gpu * world
+
+    peak, peak_kind = load_peaks()
+    tag = {"rdp": "rdp_encode_p7_config1", "rs8": "rs8_encode_6_2_config2", "xor": "xor_encode_7_config0"}[wl["scheme"]]
+    roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu / peak, 4), "traffic": traffic_from_profiles(tag),
+                "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
+                "kernel": {"rdp": "rdp_encode_kernel<7>", "rs8": "gf8_vec_kernel<2,32>",
+                           "xor": "xor_vec_kernel<4>"}[wl["scheme"]]}
+    if world > 1:
+        link = 770.0
+        t_roof = max((alg_bytes - remote_bytes) / (peak * 1e9), remote_bytes / (link * 1e9))
+        roofline["nvlink"] = {"remote_bytes_per_launch": remote_bytes, "peak_gbs_per_direction": link,
+                              "achieved_gbs": round(remote_bytes / (ms_step * 1e-3) / 1e9, 1),
+                              "roof_ms": round(t_roof * 1e3, 4), "frac_of_roof": round(t_roof * 1e3 / ms_step, 4)}
+
+    e2e = None
+    if not args.no_e2e and world == 1:
+        e2e = measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, max(3, min(args.steps, 20)))
+
+    cpu_baseline = None
+    if not args.no_cpu_baseline and rank == 0 and world == 1:
+        host = [t.cpu().numpy() for t in slots]
+        rate, reps, threads, el = cpu_encode_rate(wl, host, args.cpu_seconds)
+        cpu_baseline = {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                        "sample": f"the full workload ({k} x {nbytes} B shards) encoded {reps} times in {el:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": wl["desc"], "k": k, "m": m, "p": wl["p"],
+                       "unit": wl["unit"], "shard_bytes": nbytes, "parity_bytes": pbytes,
+                       "per_gpu_gbs": round(per_gpu, 2),
+                       "l2": f"working set {(alg_bytes) / MIB:.0f} MiB per step > 126 MB L2, no flush",
+                       "placement": "single GPU" if world == 1 else "shard j of rank c's codeword on GPU (c+j)%N"},
+            "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
+            "gpu_launches": args.steps, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if peer_group is not None:
+        peer_group.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):
+    """Same step through the host pipeline: pinned host shards in, parity out."""
+    off = __import__(PKG + ".offload", fromlist=["HostPipeline"])
+    host_data = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(spec.k)]
+    for h, d in zip(host_data, slots):
+        h.copy_(d)
+    host_par = [torch.empty(pbytes, dtype=torch.uint8, pin_memory=True) for _ in range(spec.m)]
+    pipe = off.HostPipeline(spec, nbytes, chunk_bytes=4 << 20, slots=3)
+    for _ in range(2):
+        pipe.encode(host_data, host_par)
+    torch.cuda.synchronize()
+    pipe.launches = 0
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        pipe.encode(host_data, host_par)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": round(alg_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": spec.k * nbytes, "d2h_bytes_per_step": spec.m * pbytes,
+            "ms_per_step": round(ms, 4), "steps": steps, "gpu_launches_per_step": pipe.launches // steps,
+            "path": "offload.HostPipeline: pinned host -> H2D -> gsec_encode -> D2H, 4 MiB chunks on 3 streams"}
+
+
+if __name__ == "__main__":
+    main()

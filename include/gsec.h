@@ -1,0 +1,245 @@
+/*
+ * gsec.h — C ABI of the B200 KV-cache erasure-coding engine (libgsec.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as an opaque pointer, 0 = legacy default stream), launches its
+ * kernels on that stream and returns without synchronising.  Nothing here
+ * allocates device memory; the caller owns every buffer.  Pointers to shards
+ * may point into another GPU's memory once it has been mapped with
+ * gsec_ipc_import (NVLink peer loads/stores).
+ *
+ * Return codes: GSEC_OK (0) or one of the GSEC_E* values below; the message of
+ * the last failure on the calling thread is returned by gsec_last_error().
+ *
+ * Reference interfaces replaced are cited as file:line of the reference
+ * project (GhostServe artifact); "ref-compat" entries reproduce the
+ * reference's bytes exactly, "engine" entries are the B200-native codec that
+ * the tensor-parallel hook uses.
+ */
+#ifndef GSEC_H_
+#define GSEC_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GSEC_API __attribute__((visibility("default")))
+#else
+#define GSEC_API
+#endif
+
+typedef void* gsec_stream_t; /* a cudaStream_t */
+
+enum {
+  GSEC_OK = 0,
+  GSEC_EINVAL = 1,          /* bad argument (shape, index, alignment, code parameters) */
+  GSEC_EUNRECOVERABLE = 2,  /* erasure pattern cannot be decoded by this code */
+  GSEC_ECUDA = 3,           /* a CUDA runtime call or kernel launch failed */
+  GSEC_ETIMEOUT = 4,        /* a bounded device-side wait gave up */
+  GSEC_EUNSUPPORTED = 5     /* parameters outside what this build implements */
+};
+
+enum {
+  GSEC_SCHEME_XOR = 0, /* single parity, byte-wise XOR */
+  GSEC_SCHEME_RDP = 1, /* Row-Diagonal Parity (Corbett et al., FAST'04), p prime, k <= p-1 */
+  GSEC_SCHEME_RS8 = 2  /* Reed-Solomon over GF(2^8), poly 0x11d, Cauchy generator */
+};
+
+/* Parameters of one erasure code (engine entries). */
+typedef struct gsec_code {
+  int32_t scheme;  /* GSEC_SCHEME_* */
+  int32_t k;       /* data shards (XOR: 1..32, RDP: 1..p-1, RS8: 1..32) */
+  int32_t m;       /* parity shards (XOR: 1, RDP: 2, RS8: 1..4) */
+  int32_t p;       /* RDP prime, 3..17 (ignored otherwise) */
+  int64_t unit;    /* RDP stripe unit in bytes, multiple of 16 (ignored otherwise) */
+} gsec_code;
+
+/* ------------------------------------------------------------------------- */
+/* Library                                                                    */
+/* ------------------------------------------------------------------------- */
+
+/* Message of the last failed call on this thread ("" if none). */
+GSEC_API const char* gsec_last_error(void);
+/* Library version string. */
+GSEC_API const char* gsec_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Engine: position-sliced encode / decode over per-shard pointers            */
+/* Replaces the gather + pack + parity sequence of the reference hook,        */
+/* bench_ghostserve_rdp.py:303-360 (_distributed_gather_kv,                    */
+/* _compute_parity_to_cpu), and the codec cores of                             */
+/* benchmark/xor/kernel.cu:17-88, benchmark/rs/kernel.cu:67-222.               */
+/* ------------------------------------------------------------------------- */
+
+/* Bytes of one parity shard for data shards of data_bytes bytes
+ * (RDP pads to whole stripes of (p-1)*unit bytes; XOR/RS8 do not pad). */
+GSEC_API int gsec_parity_bytes(const gsec_code* code, int64_t data_bytes, int64_t* out_bytes);
+
+/* Encode parity bytes [begin, end) of all m parity shards.
+ *   data_lo[i], data_hi[i]: data shard i is the byte string
+ *       data_lo[i][0 .. split) ++ data_hi[i][0 .. data_bytes-split)
+ *     (pass data_hi = NULL, or split >= data_bytes, for one contiguous buffer;
+ *      this lets the K and V halves of a rank's KV be one shard without a copy);
+ *     bytes past data_bytes read as zero (RDP tail stripe).
+ *   parity[j]: base of parity shard j (byte 0; only [begin, end) is written).
+ *   data_bytes and split must be multiples of 16, every pointer 16-byte aligned;
+ *   begin/end must be multiples of 16 (XOR/RS8) or of the stripe (RDP), except
+ *   that end may equal gsec_parity_bytes(). Any pointer may be a mapped peer
+ *   pointer (gsec_ipc_import). */
+GSEC_API int gsec_encode(const gsec_code* code,
+                const void* const* data_lo, const void* const* data_hi, int64_t split,
+                int64_t data_bytes, void* const* parity,
+                int64_t begin, int64_t end, gsec_stream_t stream);
+
+/* Rebuild the erased shards over byte range [begin, end).
+ *   shard_lo/shard_hi: k+m entries, data shards 0..k-1 then parity k..k+m-1,
+ *     same split convention as gsec_encode (parity shards are contiguous:
+ *     shard_hi entries for parity are ignored). Surviving shards are read,
+ *     erased shards are written (data shards only up to data_bytes).
+ *   erased: nerased distinct indices in [0, k+m); nerased <= m.
+ * Returns GSEC_EUNRECOVERABLE for patterns the code cannot decode. */
+GSEC_API int gsec_decode(const gsec_code* code,
+                void* const* shard_lo, void* const* shard_hi, int64_t split,
+                int64_t data_bytes, const int32_t* erased, int32_t nerased,
+                int64_t begin, int64_t end, gsec_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Layout: [K | V] byte stream <-> shard rows (folds the reference pack /     */
+/* unpack passes into one strided copy).                                       */
+/* ------------------------------------------------------------------------- */
+
+/* Copy the stream src0[0..len0) ++ src1[0..len1) into nrows rows of row_bytes
+ * bytes (row r at rows + r*pitch), zero-filling past the stream end.
+ * Replaces pack_kv (benchmark/xor/kernel.cu:93-119, :193-207) followed by the
+ * zero-pad copy of benchmark/xor/main.py:89-90, and pack_fp16_pair_to_u16
+ * (benchmark/rs/kernel.cu:36-49, :225-243) followed by benchmark/rs/main.py:104-108. */
+GSEC_API int gsec_rows_pack(const void* src0, int64_t len0, const void* src1, int64_t len1,
+                   void* rows, int64_t pitch, int64_t row_bytes, int32_t nrows,
+                   gsec_stream_t stream);
+
+/* Inverse of gsec_rows_pack: the first len0+len1 bytes of the row stream go to
+ * dst0[0..len0) and dst1[0..len1). Replaces unpack_kv
+ * (benchmark/xor/kernel.cu:122-146, :209-223) and u16_to_fp16_split
+ * (benchmark/rs/kernel.cu:51-64, :245-263). */
+GSEC_API int gsec_rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int32_t nrows,
+                     void* dst0, int64_t len0, void* dst1, int64_t len1,
+                     gsec_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* ref-compat: XOR (benchmark/xor/kernel.cu)                                   */
+/* ------------------------------------------------------------------------- */
+
+/* encode_xor: shards rows 0..k-1 = data_padded rows, row k = XOR of them.
+ * Rows of shard_size bytes at shards + r*pitch. Replaces encode_xor_launcher,
+ * benchmark/xor/kernel.cu:158-171 (kernel :17-41). data_padded may be NULL when
+ * the data rows are already in place in `shards` (parity only). */
+GSEC_API int gsec_xor_encode(const uint8_t* data_padded, uint8_t* shards, int32_t data_shards,
+                    int64_t shard_size, int64_t pitch, gsec_stream_t stream);
+
+/* reconstruct_xor: rebuild the one missing row (data or parity) of `shards` in
+ * place and also write it to recovered_missing (may be NULL). missing is a host
+ * array. Replaces reconstruct_xor_launcher, benchmark/xor/kernel.cu:173-191
+ * (kernel :47-88); the reference reads missing_indices from device memory. */
+GSEC_API int gsec_xor_reconstruct(uint8_t* shards, uint8_t* recovered_missing, int64_t shard_size,
+                         int64_t pitch, int32_t data_shards, const int32_t* missing,
+                         int32_t missing_count, gsec_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* ref-compat: the reference's mod-S "RDP" (benchmark/rdp/kernel.cu and the    */
+/* hook extension in bench_ghostserve_rdp.py:92-207), u16 words.               */
+/* ------------------------------------------------------------------------- */
+
+/* pack_row_from_block: row `row` of `shards` = [k_blk words | v_blk words].
+ * Replaces bench_ghostserve_rdp.py:152-175 (kernel :105-118). */
+GSEC_API int gsec_rdpref_pack_row(const uint16_t* k_blk, const uint16_t* v_blk, int64_t words,
+                         uint16_t* shards, int64_t pitch_words, int32_t row,
+                         gsec_stream_t stream);
+
+/* compute_rdp_parity: P row (nd) = XOR of data rows, Q row (nd+1) = diagonal
+ * XOR mod S skipping one star cell per row. Replaces
+ * bench_ghostserve_rdp.py:181-199 (kernel :121-150) and the parity half of
+ * fused_backup_full_kv_launcher, benchmark/rdp/kernel.cu:383-394 (kernel :76-107). */
+GSEC_API int gsec_rdpref_parity(uint16_t* rows, int64_t pitch_words, int32_t nd, int64_t S,
+                       int32_t star_base, gsec_stream_t stream);
+
+/* fused_backup_full_kv: pack the token-major stream [K_TN | V_TN] (T*n words
+ * each) into nd rows of S words and compute P/Q. Replaces
+ * fused_backup_full_kv_launcher, benchmark/rdp/kernel.cu:366-395. */
+GSEC_API int gsec_rdpref_backup(const uint16_t* k_tn, const uint16_t* v_tn, uint16_t* shards,
+                       int64_t pitch_words, int32_t nd, int64_t S, int64_t T, int64_t n,
+                       int32_t star_base, gsec_stream_t stream);
+
+/* Same as gsec_rdpref_backup but reads K and V in their [B,H,T,D] layout and
+ * applies the [T, B*H*D] permutation while packing (benchmark/rdp/main.py:66-67
+ * does it as two .contiguous() copies). */
+GSEC_API int gsec_rdpref_backup_bhtd(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H,
+                            int64_t T, int64_t D, uint16_t* shards, int64_t pitch_words,
+                            int32_t nd, int64_t S, int32_t star_base, gsec_stream_t stream);
+
+/* fused_recovery_full_kv: reproduce the reference recovery on `shards` in place
+ * and write the token-major stream [K_TN | V_TN] to out_tn. Replaces
+ * fused_recovery_full_kv_launcher, benchmark/rdp/kernel.cu:397-521. The
+ * reference's two-erasure sequence ends with rebuild_row_from_P(a) then
+ * rebuild_row_from_P(b) (:472-490), which leaves row b as it is and sets row
+ * min(a,b) = P ^ (all other rows); this entry produces exactly those bytes. */
+GSEC_API int gsec_rdpref_recovery(uint16_t* shards, int64_t pitch_words, uint16_t* out_tn,
+                         int32_t nd, int64_t S, int64_t T, int64_t n, int32_t star_base,
+                         int32_t miss_a, int32_t miss_b, gsec_stream_t stream);
+
+/* As gsec_rdpref_recovery, but writes K and V back in [B,H,T,D] layout
+ * (benchmark/rdp/main.py:121-124 does the inverse permutation as copies). */
+GSEC_API int gsec_rdpref_recovery_bhtd(uint16_t* shards, int64_t pitch_words, uint16_t* k_out,
+                              uint16_t* v_out, int64_t B, int64_t H, int64_t T, int64_t D,
+                              int32_t nd, int64_t S, int32_t star_base, int32_t miss_a,
+                              int32_t miss_b, gsec_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* ref-compat: Reed-Solomon over GF(2^16), poly 0x1100B (benchmark/rs)         */
+/* ------------------------------------------------------------------------- */
+
+/* init_gf_tables: exp (2*65535 entries) and log (65536 entries) tables, the
+ * same values benchmark/rs/main.py:39-54 builds. Host memory. */
+GSEC_API int gsec_rs16_tables(uint16_t* gf_exp, uint16_t* gf_log);
+
+/* encode_rs_u16: rows 0..k-1 of `shards` = data_padded rows (skipped when
+ * data_padded is NULL: data already in place), rows k..k+m-1 = parity
+ * P_p = sum_i alpha^((p+1)*i mod 65535) * D_i. Replaces encode_rs_u16,
+ * benchmark/rs/kernel.cu:265-285 (kernel :67-102). */
+GSEC_API int gsec_rs16_encode(const uint16_t* data_padded, uint16_t* shards, int64_t pitch_words,
+                     int32_t data_shards, int32_t parity_shards, int64_t shard_size,
+                     gsec_stream_t stream);
+
+/* reconstruct_rs_u16_inplace: rebuild the nmiss missing data rows from the
+ * parity rows parity_used[0..nmiss) (host arrays). Replaces
+ * reconstruct_rs_u16_inplace, benchmark/rs/kernel.cu:287-312 (kernel :105-222);
+ * the m x m inversion is done once on the host with the same Gauss-Jordan
+ * steps instead of once per thread block. */
+GSEC_API int gsec_rs16_reconstruct(uint16_t* shards, int64_t pitch_words, int64_t shard_size,
+                          int32_t data_shards, int32_t parity_shards,
+                          const int32_t* missing_data, int32_t nmiss,
+                          const int32_t* parity_used, gsec_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Peer mapping for the tensor-parallel path (CUDA IPC over NVLink)           */
+/* Replaces the NCCL gathers of bench_ghostserve_rdp.py:321-331: peers' KV     */
+/* is read in place by the encode kernel instead of being copied to one rank. */
+/* ------------------------------------------------------------------------- */
+
+#define GSEC_IPC_HANDLE_BYTES 64
+
+/* Export the allocation containing ptr: 64-byte handle + ptr's offset in it. */
+GSEC_API int gsec_ipc_export(const void* ptr, void* handle, int64_t* offset);
+/* Map a peer allocation (current device) and return base + offset. Mapping the
+ * same handle again returns the cached mapping. */
+GSEC_API int gsec_ipc_import(const void* handle, int64_t offset, void** ptr);
+/* Unmap every allocation mapped by gsec_ipc_import on the current device. */
+GSEC_API int gsec_ipc_close_all(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSEC_H_ */

@@ -1,0 +1,235 @@
+"""GPU parity of the engine codes (XOR, textbook RDP, RS8) against the CPU oracle.
+
+Bit-exact on seeded inputs at small sizes for every erasure pattern; at the
+BASELINE sizes (32 MiB bf16 shards) through size-independent properties:
+encode -> erase every pair -> decode returns the original bytes."""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_bits, pkg, rand_bytes
+from oracle import codes
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().numpy().view(np.uint8).reshape(-1)
+
+
+def run_roundtrip(spec, data_np, erasure_sets, data_bytes):
+    g = pkg()
+    data = [dev(d) for d in data_np]
+    par = g.encode(spec, data)
+    full = [host(t) for t in data + par]
+    for er in erasure_sets:
+        shards = [None if i in er else (data + par)[i] for i in range(spec.n)]
+        out = g.decode(spec, shards, er, data_bytes=data_bytes)
+        for i in er:
+            assert np.array_equal(host(out[i]), full[i]), (spec, er, i)
+    return full
+
+
+# ------------------------------------------------------------------- XOR -----
+@pytest.mark.parametrize("k", [1, 2, 7, 8, 16])
+@pytest.mark.parametrize("nbytes", [16, 4096, 16 * 1037])
+def test_xor_matches_oracle(rng, k, nbytes):
+    g = pkg()
+    spec = g.CodeSpec.xor(k)
+    data = [rand_bytes(rng, nbytes) for _ in range(k)]
+    full = run_roundtrip(spec, data, [[e] for e in range(k + 1)], nbytes)
+    assert np.array_equal(full[k], codes.xor_encode(data))
+
+
+# ------------------------------------------------------------------- RDP -----
+RDP_CASES = [(3, 2), (5, 4), (5, 3), (7, 6), (7, 4), (11, 8), (11, 10), (13, 12), (17, 16), (17, 9)]
+
+
+@pytest.mark.parametrize("p,k", RDP_CASES)
+@pytest.mark.parametrize("unit", [16, 4096])
+def test_rdp_encode_matches_oracle(rng, p, k, unit):
+    g = pkg()
+    spec = g.CodeSpec.rdp(k, p, unit)
+    data_bytes = 2 * (p - 1) * unit + 3 * unit + 32  # two stripes + a partial one
+    data = [rand_bytes(rng, data_bytes) for _ in range(k)]
+    P, Q = codes.rdp_encode(data, p, unit)
+    par = g.encode(spec, [dev(d) for d in data])
+    assert np.array_equal(host(par[0]), P)
+    assert np.array_equal(host(par[1]), Q)
+
+
+@pytest.mark.parametrize("p,k", RDP_CASES)
+def test_rdp_decodes_every_pattern(rng, p, k):
+    g = pkg()
+    unit = 64
+    spec = g.CodeSpec.rdp(k, p, unit)
+    data_bytes = 3 * (p - 1) * unit + 5 * 16
+    data = [rand_bytes(rng, data_bytes) for _ in range(k)]
+    pats = [list(e) for n in (1, 2) for e in itertools.combinations(range(k + 2), n)]
+    run_roundtrip(spec, data, pats, data_bytes)
+
+
+def test_rdp_decode_matches_oracle_peeling(rng):
+    # CUDA mask decoder vs the oracle's independent peeling decoder.
+    g = pkg()
+    p, k, unit = 7, 6, 4096
+    spec = g.CodeSpec.rdp(k, p, unit)
+    data_bytes = 2 * 6 * unit + 4096
+    data = [rand_bytes(rng, data_bytes) for _ in range(k)]
+    P, Q = codes.rdp_encode(data, p, unit)
+    full = data + [P, Q]
+    ddata = [dev(d) for d in data]
+    dpar = [dev(P), dev(Q)]
+    for er in itertools.combinations(range(k + 2), 2):
+        want = codes.rdp_decode([None if i in er else full[i] for i in range(k + 2)], k, p, unit, data_bytes)
+        sh = [None if i in er else (ddata + dpar)[i] for i in range(k + 2)]
+        out = g.decode(spec, sh, list(er), data_bytes=data_bytes)
+        for i in er:
+            assert np.array_equal(host(out[i]), want[i])
+
+
+# ------------------------------------------------------------------- RS8 -----
+@pytest.mark.parametrize("k,m", [(6, 2), (4, 4), (10, 3), (1, 1), (32, 4), (3, 2)])
+def test_rs8_matches_oracle_every_pattern(rng, k, m):
+    g = pkg()
+    spec = g.CodeSpec.rs8(k, m)
+    nbytes = 16 * 129
+    data = [rand_bytes(rng, nbytes) for _ in range(k)]
+    want = codes.rs8_encode(data, m)
+    pats = [list(e) for n in range(1, m + 1) for e in itertools.combinations(range(k + m), n)]
+    if len(pats) > 120:
+        pats = pats[:: len(pats) // 120 + 1] + [list(range(k, k + m)), list(range(m))]
+    full = run_roundtrip(spec, data, pats, nbytes)
+    for j in range(m):
+        assert np.array_equal(full[k + j], want[j])
+
+
+# ---------------------------------------------------- segments and ranges ----
+@pytest.mark.parametrize("scheme", ["xor", "rdp", "rs8"])
+def test_two_segment_shards_equal_concatenation(rng, scheme):
+    g = pkg()
+    k = 6
+    spec = {"xor": g.CodeSpec.xor(k), "rdp": g.CodeSpec.rdp(k, 7, 256), "rs8": g.CodeSpec.rs8(k, 2)}[scheme]
+    lo_b, hi_b = 16 * 301, 16 * 257
+    lo = [rand_bytes(rng, lo_b) for _ in range(k)]
+    hi = [rand_bytes(rng, hi_b) for _ in range(k)]
+    cat = [dev(np.concatenate([a, b])) for a, b in zip(lo, hi)]
+    pairs = [(dev(a), dev(b)) for a, b in zip(lo, hi)]
+    want = [host(t) for t in g.encode(spec, cat)]
+    got = [host(t) for t in g.encode(spec, pairs)]
+    for a, b in zip(want, got):
+        assert np.array_equal(a, b)
+    # decode a data shard back into a split destination
+    er = [1, k] if spec.m > 1 else [1]
+    par = [dev(w) for w in want]
+    dst = (torch.empty(lo_b, dtype=torch.uint8, device="cuda"), torch.empty(hi_b, dtype=torch.uint8, device="cuda"))
+    sh = [p if i not in er else None for i, p in enumerate(pairs)] + list(par)
+    sh[1] = dst
+    if k in er:
+        sh[k] = torch.empty_like(par[0])
+    out = g.decode(spec, sh, er)
+    assert np.array_equal(host(out[1][0]), lo[1]) and np.array_equal(host(out[1][1]), hi[1])
+
+
+@pytest.mark.parametrize("scheme", ["xor", "rdp", "rs8"])
+def test_range_slices_compose(rng, scheme):
+    g = pkg()
+    k = 4
+    spec = {"xor": g.CodeSpec.xor(k), "rdp": g.CodeSpec.rdp(k, 5, 64), "rs8": g.CodeSpec.rs8(k, 3)}[scheme]
+    nbytes = 4 * 256 * 7 + 64
+    data = [dev(rand_bytes(rng, nbytes)) for _ in range(k)]
+    full = [host(t) for t in g.encode(spec, data)]
+    pb = spec.parity_bytes(nbytes)
+    gran = spec.stripe_bytes()
+    cut = (pb // gran // 2) * gran
+    par = [torch.zeros(pb, dtype=torch.uint8, device="cuda") for _ in range(spec.m)]
+    g.encode(spec, data, par, 0, cut)
+    g.encode(spec, data, par, cut, pb)
+    for a, b in zip(full, par):
+        assert np.array_equal(a, host(b))
+
+
+# --------------------------------------------------------- BASELINE sizes ----
+def kv_shards_bf16(seed: int, k: int):
+    """k ranks' KV chunk: K and V [32 layers, 2048 tokens, 1 head, 128] bf16 N(0,1)."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    out = []
+    for _ in range(k):
+        kv = torch.randn(2, 32, 2048, 1, 128, generator=gen, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+        out.append(kv.view(torch.uint8).reshape(-1))
+    return out
+
+
+def test_config1_rdp_p7_full_size_all_pairs():
+    g = pkg()
+    spec = g.CodeSpec.rdp(6, 7, 4096)
+    data = kv_shards_bf16(11, 6)
+    assert data[0].numel() == 32 << 20
+    par = g.encode(spec, data)
+    assert par[0].numel() == 1366 * 6 * 4096
+    full = data + par
+    sums = [torch.sum(t.view(torch.int32).to(torch.int64)).item() for t in full]
+    for er in itertools.combinations(range(8), 2):
+        sh = [None if i in er else full[i] for i in range(8)]
+        out = g.decode(spec, sh, list(er), data_bytes=32 << 20)
+        for i in er:
+            assert torch.equal(out[i], full[i]), er
+            assert torch.sum(out[i].view(torch.int32).to(torch.int64)).item() == sums[i]
+
+
+def test_config1_matches_oracle_on_a_slice():
+    g = pkg()
+    spec = g.CodeSpec.rdp(6, 7, 4096)
+    data = kv_shards_bf16(12, 6)
+    par = g.encode(spec, data)
+    sb = 6 * 4096
+    lo, hi = 500 * sb, 503 * sb
+    want = codes.rdp_encode([host(d[lo:hi]) for d in data], 7, 4096)
+    assert np.array_equal(host(par[0][lo:hi]), want[0])
+    assert np.array_equal(host(par[1][lo:hi]), want[1])
+    # the padded tail stripe
+    tail = 1365 * sb
+    want = codes.rdp_encode([host(d[tail:]) for d in data], 7, 4096)
+    assert np.array_equal(host(par[0][tail:]), want[0])
+    assert np.array_equal(host(par[1][tail:]), want[1])
+
+
+def test_config2_rs8_fp8_full_size_all_pairs():
+    g = pkg()
+    spec = g.CodeSpec.rs8(6, 2)
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    data = [torch.randint(0, 256, (16 << 20,), generator=gen, device="cuda", dtype=torch.uint8) for _ in range(6)]
+    par = g.encode(spec, data)
+    full = data + par
+    for er in itertools.combinations(range(8), 2):
+        out = g.decode(spec, [None if i in er else full[i] for i in range(8)], list(er), data_bytes=16 << 20)
+        for i in er:
+            assert torch.equal(out[i], full[i]), er
+    lo = 4096 * 100
+    want = codes.rs8_encode([host(d[lo:lo + 4096]) for d in data], 2)
+    assert np.array_equal(host(par[0][lo:lo + 4096]), want[0])
+    assert np.array_equal(host(par[1][lo:lo + 4096]), want[1])
+
+
+def test_config0_xor_full_size():
+    g = pkg()
+    spec = g.CodeSpec.xor(7)
+    data = kv_shards_bf16(3, 7)
+    par = g.encode(spec, data)
+    x = data[0].clone()
+    for d in data[1:]:
+        x ^= d
+    assert torch.equal(x, par[0])
+    gen = np.random.default_rng(5)
+    e = int(gen.integers(0, 8))
+    full = data + par
+    out = g.decode(spec, [None if i == e else full[i] for i in range(8)], [e], data_bytes=32 << 20)
+    assert torch.equal(out[e], full[e])
