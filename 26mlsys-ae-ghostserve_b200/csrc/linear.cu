@@ -230,7 +230,8 @@ __global__ void __launch_bounds__(256) linear_scalar_kernel(const LinearPass a) 
 }
 
 bool pass_aligned(const LinearPass& a) {
-  if ((a.begin & 15) || (a.split & 15)) return false;
+  // a split at or past the end of the range (contiguous shards) never takes effect
+  if ((a.begin & 15) || (a.split < a.end && (a.split & 15))) return false;
   for (int i = 0; i < a.nin; ++i)
     if (!aligned16(a.in_lo[i]) || !aligned16(a.in_hi[i])) return false;
   for (int j = 0; j < a.nout; ++j)

@@ -1,0 +1,394 @@
+"""Drop-in for the reference's KV fault-tolerance hook on SGLang's FlashInfer
+backend (bench_ghostserve_rdp.py:212-532).
+
+``patch_backend(backend, ft)`` replaces ``backend.forward_extend`` exactly like
+``_patch_flashinfer_backend`` (:396-481): the wrapper forwards every argument,
+always returns the original result and swallows (and logs) any error of the
+fault-tolerance work.  After each extend call, ``ft.on_extend`` takes the
+prefill-delta KV (``kv_pool[slot_mapping != -1]``, :440-458) and protects it:
+
+mode="reference"  the reference flow, bit for bit: chunk id from rank 0
+                  (:287-301), NCCL gather of every rank's K and V to the
+                  rotating destination rank (:303-332), fp16 value cast, pack,
+                  mod-S row/diagonal parity and a copy of P and Q to the host
+                  (:334-392) — with libgsec's kernels instead of the JIT ones.
+mode="fused"      the B200 path: every rank stages its delta KV in a buffer the
+                  other ranks have mapped (CUDA IPC); after one stream-ordered
+                  barrier each rank encodes its 1/world slice of the stripes,
+                  reading all ranks' KV with NVLink peer loads inside the encode
+                  kernel, and offloads its parity slice to pinned host memory
+                  asynchronously.  No gather, no value cast (raw KV bytes), no
+                  host sync besides the active-slot count.
+
+Both modes append the reference's JSONL record (:377-389) to FT_METRICS_FILE.
+"""
+from __future__ import annotations
+
+import functools
+import json
+import os
+import time
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import codec, ext
+
+ENV_FLAG = "SGLANG_GATHER_KV_TO_GPU0"
+LOG_PREFIX = "[ft-rdp]"
+
+
+def _log(msg: str) -> None:
+    try:
+        print(f"{LOG_PREFIX} {msg}", flush=True)
+    except Exception:
+        pass
+
+
+@dataclass
+class HookConfig:
+    mode: str = "fused"                 # "fused" | "reference"
+    scheme: str = "rdp"                 # fused mode code: "rdp" | "xor" | "rs8"
+    rs_parity: int = 2
+    unit: int = 4096                    # RDP stripe unit
+    star_base: int = field(default_factory=lambda: int(os.getenv("RDP_STAR_BASE", "0")))
+    metrics_file: Optional[str] = field(default_factory=lambda: os.getenv("FT_METRICS_FILE"))
+    prog_start_mono: float = field(default_factory=lambda: float(os.getenv("FT_PROG_START_MONO", "nan")))
+    compat_cast_fp16: bool = True       # reference mode: .to(float16) as bench_ghostserve_rdp.py:345-346
+    broadcast_chunk_id: bool = True     # reference mode: rank-0 counter + broadcast (:287-301)
+    offload: bool = True                # copy parity to pinned host memory
+    host_ring: int = 4                  # pinned parity buffers kept per rank
+    verbose: bool = False
+
+
+class KVFaultTolerance:
+    """Per-process state of the hook (the module globals of the reference plugin)."""
+
+    def __init__(self, config: Optional[HookConfig] = None, group=None):
+        self.cfg = config or HookConfig()
+        self.group = group
+        self.chunk_counter = 0
+        self.first_chunk_wall_ms = None
+        self.records = []
+        self._staging = None      # fused mode: registered KV staging (2 slots)
+        self._peers = None
+        self._parity = None
+        self._host = []
+        self._pending = []        # (record, event, t_enqueue) awaiting D2H completion
+        self._copy_stream = None
+        self._calls = 0
+
+    # ------------------------------------------------------------- control --
+    def _rank_world(self):
+        return dist.get_rank(self.group), dist.get_world_size(self.group)
+
+    def next_chunk_id(self, device=None):
+        """(chunk_id, dst_rank) with dst = (chunk_id - 1) % world (:287-301)."""
+        rank, world = self._rank_world()
+        if self.cfg.mode == "reference" and self.cfg.broadcast_chunk_id:
+            if rank == 0:
+                self.chunk_counter += 1
+            t = torch.tensor([self.chunk_counter], device=device, dtype=torch.int64)
+            dist.broadcast(t, src=dist.get_global_rank(self.group, 0) if self.group else 0, group=self.group)
+            cid = int(t.item())
+            self.chunk_counter = cid
+        else:
+            # every rank runs the hook once per extend call, so a local counter
+            # gives the same id everywhere without a broadcast or a host sync
+            self.chunk_counter += 1
+            cid = self.chunk_counter
+        return cid, (cid - 1) % world
+
+    def _barrier(self, device):
+        """Stream-ordered on NCCL (a 1-element all-reduce); host-side otherwise."""
+        if dist.get_backend(self.group) == "nccl":
+            t = torch.zeros(1, device=device)
+            dist.all_reduce(t, group=self.group)
+        else:
+            torch.cuda.current_stream(device).synchronize()
+            dist.barrier(group=self.group)
+
+    # ---------------------------------------------------- reference flow ----
+    def gather_kv(self, local_k, local_v, dst_rank):
+        """_distributed_gather_kv, bench_ghostserve_rdp.py:303-332."""
+        rank, world = self._rank_world()
+        kf = local_k.contiguous().view(-1)
+        vf = local_v.contiguous().view(-1)
+        elems = int(kf.numel())
+        if elems == 0:
+            return None
+        dst = dist.get_global_rank(self.group, dst_rank) if self.group else dst_rank
+        if rank == dst_rank:
+            k_all = torch.empty(elems * world, dtype=kf.dtype, device=kf.device)
+            v_all = torch.empty(elems * world, dtype=vf.dtype, device=vf.device)
+            dist.gather(kf, gather_list=[k_all.narrow(0, i * elems, elems) for i in range(world)], dst=dst,
+                        group=self.group)
+            dist.gather(vf, gather_list=[v_all.narrow(0, i * elems, elems) for i in range(world)], dst=dst,
+                        group=self.group)
+            return k_all, v_all, elems
+        dist.gather(kf, gather_list=None, dst=dst, group=self.group)
+        dist.gather(vf, gather_list=None, dst=dst, group=self.group)
+        return None
+
+    def compute_parity_to_cpu(self, K_all, V_all, elems, chunk_id, dst_rank):
+        """_compute_parity_to_cpu, bench_ghostserve_rdp.py:334-392, on libgsec."""
+        world = int(K_all.numel() // elems)
+        S = 2 * elems
+        rows = torch.empty((world + 2, S), dtype=torch.uint16, device=K_all.device)
+        for r in range(world):
+            k = K_all.narrow(0, r * elems, elems)
+            v = V_all.narrow(0, r * elems, elems)
+            if self.cfg.compat_cast_fp16:
+                k, v = k.to(torch.float16), v.to(torch.float16)
+            ext.rdp_kv_ops.pack_row_from_block(k.view(1, 1, elems, 1), v.view(1, 1, elems, 1), rows, r)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ext.rdp_kv_ops.compute_rdp_parity(rows, nd=world, S=S, star_base=self.cfg.star_base)
+        e1.record()
+        torch.cuda.synchronize()
+        encode_ms = float(e0.elapsed_time(e1))
+        t0 = time.perf_counter()
+        P_cpu = rows[world].to("cpu", non_blocking=True).contiguous()
+        Q_cpu = rows[world + 1].to("cpu", non_blocking=True).contiguous()
+        torch.cuda.synchronize()
+        d2h_ms = (time.perf_counter() - t0) * 1000.0
+        t1 = time.perf_counter()
+        _ = P_cpu.to(rows.device, non_blocking=True)
+        _ = Q_cpu.to(rows.device, non_blocking=True)
+        torch.cuda.synchronize()
+        h2d_ms = (time.perf_counter() - t1) * 1000.0
+        rec = self._record(chunk_id, dst_rank, encode_ms, d2h_ms, h2d_ms, int((P_cpu.numel() + Q_cpu.numel()) * 2))
+        self._emit(rec)
+        return P_cpu, Q_cpu
+
+    # -------------------------------------------------------- fused flow ----
+    def _spec(self, world: int) -> codec.CodeSpec:
+        if self.cfg.scheme == "xor":
+            return codec.CodeSpec.xor(world)
+        if self.cfg.scheme == "rs8":
+            return codec.CodeSpec.rs8(world, self.cfg.rs_parity)
+        return codec.CodeSpec.rdp(world, unit=self.cfg.unit)
+
+    def _ensure_staging(self, nbytes_half: int, device):
+        from . import p2p
+
+        rank, world = self._rank_world()
+        if self._staging is not None and self._staging[0][0].numel() >= nbytes_half:
+            return
+        if self._peers is not None:
+            self._barrier(device)
+            torch.cuda.synchronize(device)
+            self._peers.close()
+        cap = max(nbytes_half, 1 << 20)
+        cap = -(-cap // 4096) * 4096
+        # two slots, each a K buffer and a V buffer; peers read them in place
+        self._staging = [[torch.empty(cap, dtype=torch.uint8, device=device) for _ in range(2)] for _ in range(2)]
+        flat = [t for slot in self._staging for t in slot]
+        self._peers = p2p.PeerGroup.create(flat, group=self.group)
+
+    def encode_chunk(self, local_k: torch.Tensor, local_v: torch.Tensor, chunk_id: int):
+        """Fused P2P encode of this rank's slice; returns the device parity slices."""
+        from . import p2p
+
+        rank, world = self._rank_world()
+        device = local_k.device
+        kb = local_k.contiguous().view(torch.uint8).reshape(-1)
+        vb = local_v.contiguous().view(torch.uint8).reshape(-1)
+        half = kb.numel()
+        if half % 16 or vb.numel() != half:
+            raise ValueError("delta K and V must have equal sizes, multiples of 16 bytes")
+        self._ensure_staging(half, device)
+        slot = self._calls % 2
+        self._calls += 1
+        self._staging[slot][0][:half].copy_(kb)
+        self._staging[slot][1][:half].copy_(vb)
+        self._barrier(device)  # every rank's staging write precedes every peer read
+        spec = self._spec(world)
+        data_bytes = 2 * half
+        pbytes = spec.parity_bytes(data_bytes)
+        g = spec.stripe_bytes()
+        lo, hi = p2p.stripe_slice(rank, world, pbytes // g)
+        lo, hi = lo * g, hi * g
+        if self._parity is None or self._parity[0].numel() < max(hi - lo, 16):
+            self._parity = [torch.empty(max(hi - lo, 16), dtype=torch.uint8, device=device) for _ in range(spec.m)]
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if hi > lo:
+            data_lo = [self._peers.ptr(r, 2 * slot) for r in range(world)]
+            data_hi = [self._peers.ptr(r, 2 * slot + 1) for r in range(world)]
+            codec.encode_ptrs(spec, data_lo, data_hi, half, data_bytes,
+                              [t.data_ptr() - lo for t in self._parity], lo, hi)
+        e1.record()
+        rec = self._record(chunk_id, -1, None, None, None, spec.m * (hi - lo))
+        rec["slice"] = [lo, hi]
+        rec["scheme"] = spec.scheme
+        if self.cfg.offload and hi > lo:
+            self._offload(rec, [t[:hi - lo] for t in self._parity], e0, e1)
+        else:
+            self._pending.append((rec, None, e0, e1))
+        self._drain(block=False)
+        return [t[:hi - lo] for t in self._parity], (lo, hi)
+
+    def _offload(self, rec, parity, e0, e1):
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(parity[0].device)
+        nbytes = sum(t.numel() for t in parity)
+        cur = torch.cuda.current_stream(parity[0].device)
+        self._copy_stream.wait_stream(cur)
+        ring_slot = None
+        if len(self._host) < self.cfg.host_ring:
+            ring_slot = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+            self._host.append(ring_slot)
+        else:
+            ring_slot = self._host[self._calls % len(self._host)]
+            if ring_slot.numel() < nbytes:
+                ring_slot = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+                self._host[self._calls % len(self._host)] = ring_slot
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self._copy_stream):
+            d0.record()
+            off = 0
+            for t in parity:
+                ring_slot[off:off + t.numel()].copy_(t, non_blocking=True)
+                off += t.numel()
+            d1.record()
+        # the parity buffer is reused next call: order the next encode after this copy
+        cur.wait_stream(self._copy_stream)
+        rec["host_parity"] = ring_slot
+        self._pending.append((rec, (d0, d1), e0, e1))
+
+    def _drain(self, block: bool):
+        keep = []
+        for rec, d2h, e0, e1 in self._pending:
+            if not block and not e1.query():
+                keep.append((rec, d2h, e0, e1))
+                continue
+            if block:
+                e1.synchronize()
+            rec["timings"]["rdp_encode_ms"] = float(e0.elapsed_time(e1))
+            if d2h is not None:
+                if not block and not d2h[1].query():
+                    keep.append((rec, d2h, e0, e1))
+                    continue
+                d2h[1].synchronize()
+                rec["timings"]["gpu_to_cpu_ms"] = float(d2h[0].elapsed_time(d2h[1]))
+            rec.pop("host_parity", None)
+            self._emit(rec)
+        self._pending = keep
+
+    def flush(self):
+        """Wait for outstanding encodes/offloads and emit their records."""
+        self._drain(block=True)
+
+    def close(self):
+        self.flush()
+        if self._peers is not None:
+            dev = self._staging[0][0].device
+            self._barrier(dev)
+            torch.cuda.synchronize(dev)
+            self._peers.close()
+            self._peers = None
+
+    # ------------------------------------------------------------ metrics ----
+    def _record(self, chunk_id, dst_rank, enc_ms, d2h_ms, h2d_ms, parity_bytes):
+        return {
+            "chunk_id": int(chunk_id),
+            "dst_rank": int(dst_rank),
+            "first_chunk_wall_ms": None if self.first_chunk_wall_ms is None else float(self.first_chunk_wall_ms),
+            "timings": {"rdp_encode_ms": enc_ms, "rdp_decode_ms": None, "gpu_to_cpu_ms": d2h_ms,
+                        "cpu_to_gpu_ms": h2d_ms, "parity_bytes": int(parity_bytes)},
+        }
+
+    def _emit(self, rec):
+        self.records.append(rec)
+        if self.cfg.metrics_file:
+            try:
+                with open(self.cfg.metrics_file, "a", encoding="utf-8") as f:
+                    f.write(json.dumps(rec) + "\n")
+            except Exception:
+                pass
+        if self.cfg.verbose:
+            t = rec["timings"]
+            _log(f"chunk={rec['chunk_id']} dst={rec['dst_rank']} encode={t['rdp_encode_ms']}ms "
+                 f"D2H={t['gpu_to_cpu_ms']}ms parity={t['parity_bytes'] / 2**20:.3f}MiB")
+
+    # ------------------------------------------------------------ the hook --
+    def on_extend(self, batch, kv_pool) -> None:
+        """Protect the delta KV of one extend call (bench_ghostserve_rdp.py:428-471)."""
+        if not (dist.is_available() and dist.is_initialized()):
+            return
+        slots = getattr(batch, "slot_mapping", None)
+        if slots is None:
+            return
+        if not isinstance(slots, torch.Tensor):
+            slots = torch.as_tensor(slots, device=kv_pool.device)
+        active = slots != -1
+        if int(active.sum().item()) == 0:
+            return
+        active_slots = slots[active].to(dtype=torch.long)
+        local_k = kv_pool[active_slots, 0].contiguous()
+        local_v = kv_pool[active_slots, 1].contiguous()
+        chunk_id, dst_rank = self.next_chunk_id(device=local_k.device)
+        if self.first_chunk_wall_ms is None and self.cfg.prog_start_mono == self.cfg.prog_start_mono:
+            self.first_chunk_wall_ms = (time.perf_counter() - self.cfg.prog_start_mono) * 1000.0
+        if self.cfg.mode == "reference":
+            gathered = self.gather_kv(local_k, local_v, dst_rank)
+            if gathered is not None:
+                self.compute_parity_to_cpu(*gathered, chunk_id, dst_rank)
+        else:
+            self.encode_chunk(local_k, local_v, chunk_id)
+
+
+def patch_backend(backend, ft: KVFaultTolerance) -> bool:
+    """_patch_flashinfer_backend, bench_ghostserve_rdp.py:396-481."""
+    if getattr(backend, "_gsec_patched", False):
+        return True
+    if "FlashInfer" not in backend.__class__.__name__:
+        _log(f"SKIP: backend is {backend.__class__.__name__}, not FlashInfer")
+        return False
+    if not hasattr(backend, "forward_extend"):
+        _log("SKIP: FlashInfer backend missing forward_extend")
+        return False
+    orig = backend.forward_extend
+
+    @functools.wraps(orig)
+    def hooked_forward_extend(*args, **kwargs):
+        res = orig(*args, **kwargs)
+        try:
+            batch = kwargs.get("batch", None)
+            if batch is None and len(args) >= 1:
+                batch = args[0]
+            if batch is None:
+                return res
+            # The reference chains these with `or` (bench_ghostserve_rdp.py:441), which
+            # asks a multi-element tensor for its truth value and raises, so its hook
+            # gives up whenever the pool is found as kv_buffer or kv_pool.
+            kv_pool = None
+            for name in ("kv_buffer", "kv_pool", "kv_cache"):
+                kv_pool = getattr(backend, name, None)
+                if kv_pool is not None:
+                    break
+            if kv_pool is None:
+                return res
+            ft.on_extend(batch, kv_pool)
+        except Exception as e:  # the hook never breaks the model's forward pass
+            _log(f"FlashInfer hook error: {e}")
+        return res
+
+    backend.forward_extend = hooked_forward_extend
+    backend._gsec_patched = True
+    _log("Successfully hooked FlashInferAttnBackend.forward_extend")
+    return True
+
+
+def patch_model_runner(model_runner, ft: KVFaultTolerance) -> bool:
+    """Find the attention backend of a ModelRunner and patch it (:405-411)."""
+    backend = getattr(model_runner, "attn_backend", None) or getattr(model_runner, "attention_backend", None)
+    if backend is None:
+        return False
+    return patch_backend(backend, ft)

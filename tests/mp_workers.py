@@ -1,0 +1,152 @@
+"""Worker functions for multi-process tests (importable by spawned children)."""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def _init(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+
+def _pkg(sub=""):
+    import importlib
+
+    return importlib.import_module("26mlsys-ae-ghostserve_b200" + ("." + sub if sub else ""))
+
+
+# ------------------------------------------------------------- CPU (gloo) ----
+def chunk_ids(rank, world, port, mode, out):
+    _init(rank, world, port)
+    hook = _pkg("hook")
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode=mode, metrics_file=None))
+    ids = [ft.next_chunk_id(device=None) for _ in range(5)]
+    out.put((rank, ids))
+    dist.destroy_process_group()
+
+
+def gather(rank, world, port, out):
+    _init(rank, world, port)
+    hook = _pkg("hook")
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="reference", metrics_file=None))
+    k = torch.full((3, 1, 4), rank, dtype=torch.float16)
+    v = torch.full((3, 1, 4), 10 + rank, dtype=torch.float16)
+    for dst in range(world):
+        res = ft.gather_kv(k, v, dst)
+        if rank == dst:
+            k_all, v_all, elems = res
+            out.put((rank, dst, elems, k_all.tolist(), v_all.tolist()))
+        else:
+            assert res is None
+    dist.destroy_process_group()
+
+
+def peer_table(rank, world, port, out):
+    _init(rank, world, port)
+    p2p = _pkg("p2p")
+    bufs = [torch.zeros(16 * (j + 1), dtype=torch.uint8) for j in range(3)]
+    exporter = lambda t: (bytes([rank]) * 64, t.numel())  # noqa: E731  (fake handle: owner rank)
+    importer = lambda h, off: 1000 * h[0] + off  # noqa: E731
+    grp = p2p.PeerGroup.create(bufs, exporter=exporter, importer=importer, closer=lambda: None)
+    out.put((rank, grp.table))
+    grp.close()
+    dist.destroy_process_group()
+
+
+# ----------------------------------------------- GPU (2 processes, 1 GPU) ----
+def ipc_sliced_encode(rank, world, port, scheme, out):
+    """Each rank stages a KV shard in IPC-shared memory; every rank encodes its
+    stripe slice reading all shards through mapped pointers; rank 0 assembles
+    the slices and checks them against the oracle."""
+    _init(rank, world, port)
+    torch.cuda.set_device(0)
+    g = _pkg()
+    p2p = _pkg("p2p")
+    from oracle import codes
+
+    rng = np.random.default_rng(100 + rank)
+    half = 16 * 1000 + 4096
+    k_host = rng.integers(0, 256, half, dtype=np.uint8)
+    v_host = rng.integers(0, 256, half, dtype=np.uint8)
+    kt = torch.from_numpy(k_host).cuda()
+    vt = torch.from_numpy(v_host).cuda()
+    grp = p2p.PeerGroup.create([kt, vt])
+    torch.cuda.synchronize()
+    dist.barrier()
+    spec = {"rdp": g.CodeSpec.rdp(world, unit=256), "xor": g.CodeSpec.xor(world), "rs8": g.CodeSpec.rs8(world, 2)}[
+        scheme]
+    data_bytes = 2 * half
+    pb = spec.parity_bytes(data_bytes)
+    gran = spec.stripe_bytes()
+    lo, hi = p2p.stripe_slice(rank, world, pb // gran)
+    lo, hi = lo * gran, hi * gran
+    par = [torch.zeros(max(hi - lo, 16), dtype=torch.uint8, device="cuda") for _ in range(spec.m)]
+    g.codec.encode_ptrs(spec, [grp.ptr(r, 0) for r in range(world)], [grp.ptr(r, 1) for r in range(world)], half,
+                        data_bytes, [t.data_ptr() - lo for t in par], lo, hi)
+    torch.cuda.synchronize()
+    mine = [t[:hi - lo].cpu() for t in par]
+    kv = torch.from_numpy(np.concatenate([k_host, v_host]))
+    all_kv = [torch.empty_like(kv) for _ in range(world)]
+    dist.all_gather(all_kv, kv)
+    sizes = [None] * world
+    dist.all_gather_object(sizes, (lo, hi))
+    slices = [None] * world
+    dist.all_gather_object(slices, [m.numpy() for m in mine])
+    ok = True
+    if rank == 0:
+        data = [a.numpy() for a in all_kv]
+        if scheme == "rdp":
+            want = codes.rdp_encode(data, spec.p, spec.unit)
+        elif scheme == "xor":
+            want = [codes.xor_encode(data)]
+        else:
+            want = codes.rs8_encode(data, 2)
+        for j in range(spec.m):
+            got = np.concatenate([slices[r][j] for r in range(world)])
+            ok = ok and np.array_equal(got, want[j])
+    dist.barrier()
+    grp.close()
+    out.put((rank, ok))
+    dist.destroy_process_group()
+
+
+def hook_fused(rank, world, port, out):
+    """The hook's fused mode end to end on 2 processes sharing one GPU."""
+    _init(rank, world, port)
+    torch.cuda.set_device(0)
+    hook = _pkg("hook")
+    from oracle import codes
+
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme="rdp", unit=512, metrics_file=None))
+    rng = np.random.default_rng(7 + rank)
+    ok = True
+    for step in range(3):
+        tokens = 64 + 32 * step
+        k = torch.from_numpy(rng.standard_normal((tokens, 1, 128)).astype(np.float32)).cuda().to(torch.bfloat16)
+        v = torch.from_numpy(rng.standard_normal((tokens, 1, 128)).astype(np.float32)).cuda().to(torch.bfloat16)
+        par, (lo, hi) = ft.encode_chunk(k, v, step + 1)
+        torch.cuda.synchronize()
+        shard = torch.cat([k.view(torch.uint8).reshape(-1), v.view(torch.uint8).reshape(-1)]).cpu()
+        shards = [torch.empty_like(shard) for _ in range(world)]
+        dist.all_gather(shards, shard)
+        got = [None] * world
+        dist.all_gather_object(got, [p.cpu().numpy() for p in par])
+        if rank == 0:
+            spec = ft._spec(world)
+            want = codes.rdp_encode([s.numpy() for s in shards], spec.p, spec.unit)
+            for j in range(2):
+                ok = ok and np.array_equal(np.concatenate([got[r][j] for r in range(world)]), want[j])
+    ft.close()
+    recs = [r["chunk_id"] for r in ft.records]
+    out.put((rank, ok, recs))
+    dist.destroy_process_group()

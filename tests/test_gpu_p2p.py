@@ -1,0 +1,25 @@
+"""Multi-process path on one GPU: two ranks share KV through CUDA IPC and each
+encodes its stripe slice by reading the other's memory through mapped pointers
+(the kernel path used over NVLink on several GPUs). gloo carries control only;
+nothing waits on a device flag."""
+from __future__ import annotations
+
+import pytest
+
+import mp_workers
+from test_hook import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("scheme", ["rdp", "xor", "rs8"])
+def test_ipc_sliced_encode_two_ranks(scheme):
+    res = run_ranks(mp_workers.ipc_sliced_encode, 2, scheme, timeout=300)
+    assert res[0][1] is True
+
+
+def test_hook_fused_mode_two_ranks():
+    res = run_ranks(mp_workers.hook_fused, 2, timeout=300)
+    assert res[0][1] is True
+    for _rank, _ok, recs in res:
+        assert recs == [1, 2, 3]
