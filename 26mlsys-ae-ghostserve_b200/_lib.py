@@ -59,6 +59,7 @@ _PI32 = C.POINTER(C.c_int32)
 _SIGS = {
     "gsec_last_error": (C.c_char_p, []),
     "gsec_version": (C.c_char_p, []),
+    "gsec_device_status": (C.c_int, [C.POINTER(C.c_uint32), _I32]),
     "gsec_parity_bytes": (C.c_int, [C.POINTER(Code), _I64, C.POINTER(_I64)]),
     "gsec_encode": (C.c_int, [C.POINTER(Code), _PP, _PP, _I64, _I64, _PP, _I64, _I64, _P]),
     "gsec_decode": (C.c_int, [C.POINTER(Code), _PP, _PP, _I64, _I64, _PI32, _I32, _I64, _I64, _P]),

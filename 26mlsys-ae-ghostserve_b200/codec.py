@@ -139,6 +139,45 @@ def decode_ptrs(spec: CodeSpec, shard_lo: Sequence[int], shard_hi: Optional[Sequ
               _lib.C.c_void_p(stream if stream is not None else stream_handle()))
 
 
+class PreparedEncode:
+    """One gsec_encode call with its arguments marshalled once.
+
+    For loops that encode the same buffers repeatedly (every prefill chunk of
+    the hook, the benchmark): calling it costs one ctypes call (~3 us of host
+    time) instead of rebuilding the pointer arrays each time."""
+
+    def __init__(self, spec: CodeSpec, data_lo: Sequence[int], data_hi: Optional[Sequence[int]], split: int,
+                 data_bytes: int, parity: Sequence[int], begin: int = 0, end: Optional[int] = None,
+                 stream: Optional[int] = None):
+        self._fn = _lib.lib().gsec_encode
+        self._code = spec.c_code()
+        self._args = (_lib.C.byref(self._code), _lib.ptr_array(data_lo),
+                      _lib.ptr_array(data_hi) if data_hi is not None else None, int(split), int(data_bytes),
+                      _lib.ptr_array(parity), int(begin), int(spec.parity_bytes(data_bytes) if end is None else end),
+                      _lib.C.c_void_p(stream if stream is not None else stream_handle()))
+
+    def __call__(self) -> None:
+        _lib.check(self._fn(*self._args))
+
+
+class PreparedDecode:
+    """One gsec_decode call with its arguments marshalled once."""
+
+    def __init__(self, spec: CodeSpec, shard_lo: Sequence[int], shard_hi: Optional[Sequence[int]], split: int,
+                 data_bytes: int, erased: Sequence[int], begin: int = 0, end: Optional[int] = None,
+                 stream: Optional[int] = None):
+        self._fn = _lib.lib().gsec_decode
+        self._code = spec.c_code()
+        self._args = (_lib.C.byref(self._code), _lib.ptr_array(shard_lo),
+                      _lib.ptr_array(shard_hi) if shard_hi is not None else None, int(split), int(data_bytes),
+                      _lib.i32_array(erased), len(erased), int(begin),
+                      int(spec.parity_bytes(data_bytes) if end is None else end),
+                      _lib.C.c_void_p(stream if stream is not None else stream_handle()))
+
+    def __call__(self) -> None:
+        _lib.check(self._fn(*self._args))
+
+
 def encode(spec: CodeSpec, data: Sequence[ShardLike], parity: Optional[List[torch.Tensor]] = None,
            begin: int = 0, end: Optional[int] = None,
            stream: Optional[torch.cuda.Stream] = None) -> List[torch.Tensor]:
@@ -198,6 +237,14 @@ def decode(spec: CodeSpec, shards: List[Optional[ShardLike]], erased: Sequence[i
             his.append(None)
     decode_ptrs(spec, los, his, split, data_bytes, erased, begin, end, stream_handle(stream))
     return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronise the current device and return its libgsec status word
+    (0 = every bounded wait since the last clear completed)."""
+    v = _lib.C.c_uint32(0)
+    _lib.call("gsec_device_status", _lib.C.byref(v), int(bool(clear)))
+    return int(v.value)
 
 
 def parity_bytes(spec: CodeSpec, data_bytes: int) -> int:

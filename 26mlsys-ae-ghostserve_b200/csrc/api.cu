@@ -41,6 +41,11 @@ int check_launch(const char* what) {
   return GSEC_OK;
 }
 
+int current_device() {
+  int dev = -1;
+  return cudaGetDevice(&dev) == cudaSuccess ? dev : -1;
+}
+
 int sm_count() {
   static int cache[64] = {0};
   int dev = 0;
@@ -225,6 +230,20 @@ extern "C" {
 
 const char* gsec_last_error(void) { return last_error(); }
 const char* gsec_version(void) { return "gsec 0.1.0 (sm_100a)"; }
+
+int gsec_device_status(uint32_t* status, int32_t clear) {
+  GSEC_REQUIRE(status != nullptr, "status is null");
+  if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("device synchronize");
+  const unsigned v1 = rdp_device_status(clear != 0);
+  const unsigned v2 = linear_device_status(clear != 0);
+  const unsigned v = (v1 == 0xffffffffu || v2 == 0xffffffffu) ? 0xffffffffu : (v1 | (v2 << 8));
+  if (v == 0xffffffffu) {
+    set_error("cannot read the device status word");
+    return GSEC_ECUDA;
+  }
+  *status = v;
+  return GSEC_OK;
+}
 
 int gsec_parity_bytes(const gsec_code* code, int64_t data_bytes, int64_t* out) {
   int rc = check_code(code);

@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/gsec.h"
@@ -36,31 +37,45 @@ int sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Per-device cache of a kernel's launch shape: the dynamic shared memory
+// attribute is raised once and resident-CTA counts are queried once per
+// shared-memory size, instead of on every launch.
+int current_device();
+
+struct LaunchCache {
+  static constexpr int kDevices = 64;
+  static constexpr int kSlots = 8;
+  size_t attr_smem[kDevices] = {};
+  size_t smem[kDevices][kSlots] = {};
+  int per_sm[kDevices][kSlots] = {};
+  std::mutex mu;
+
+  template <typename K>
+  int blocks_per_sm(K kernel, int threads, size_t dyn_smem) {
+    std::lock_guard<std::mutex> lock(mu);
+    const int dev = current_device();
+    if (dev < 0 || dev >= kDevices) return -1;
+    if (dyn_smem > attr_smem[dev]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem) != cudaSuccess)
+        return -1;
+      attr_smem[dev] = dyn_smem;
+    }
+    for (int i = 0; i < kSlots; ++i)
+      if (per_sm[dev][i] > 0 && smem[dev][i] == dyn_smem) return per_sm[dev][i];
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, dyn_smem) != cudaSuccess) return -1;
+    if (n < 1) n = 1;
+    for (int i = 0; i < kSlots; ++i)
+      if (per_sm[dev][i] == 0) {
+        smem[dev][i] = dyn_smem;
+        per_sm[dev][i] = n;
+        break;
+      }
+    return n;
+  }
+};
+
 // ---------------------------------------------------------- vector access ---
-
-// 16-byte global load that bypasses L1 allocation: every byte of a shard is
-// read once, so caching it in L1 only evicts useful lines.
-__device__ __forceinline__ uint4 ld_stream(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// 16-byte global load through the coherent path (peer memory written by another
-// GPU during this kernel's lifetime is not assumed; used where the read-only
-// path would be unsafe because the same buffer is written by the kernel).
-__device__ __forceinline__ uint4 ld_plain(const void* p) {
-  return *reinterpret_cast<const uint4*>(p);
-}
-
-// 16-byte streaming store (evict-first: parity is not re-read by this kernel).
-__device__ __forceinline__ void st_stream(void* p, uint4 v) {
-  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
-}
 
 __device__ __forceinline__ uint4 vxor(uint4 a, uint4 b) {
   return make_uint4(a.x ^ b.x, a.y ^ b.y, a.z ^ b.z, a.w ^ b.w);

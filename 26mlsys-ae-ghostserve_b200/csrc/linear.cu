@@ -12,6 +12,7 @@
 // replicated R times and lane l reads copy l % R: with R = 32 the 32 lanes of a
 // warp always hit 32 different banks whatever the data bytes are.
 #include "linear.cuh"
+#include "pipe.cuh"
 
 namespace gsec {
 namespace {
@@ -67,35 +68,158 @@ __device__ void linear_tail(const LinearPass& a, int64_t t0) {
   }
 }
 
-// ----------------------------------------------------------------- XOR ------
-// every output = XOR of all inputs (extra outputs receive copies).  VPT independent 16-byte vectors per thread
-// per step keep nin*VPT loads in flight.
-template <int VPT>
-__global__ void __launch_bounds__(256) xor_vec_kernel(const LinearPass a) {
+// ------------------------------------------------------- XOR (TMA ring) -----
+// Work item = one 1 KiB segment of the range; a ring stage holds that segment
+// of every input (nin x 1 KiB), filled by bulk copies from a producer lane and
+// XORed by 64 consumer threads (16 bytes each), which store every output.
+constexpr int kLSeg = 1024;
+constexpr int kLLanes = kLSeg / 16;
+constexpr int kLStages = 3;
+static __device__ unsigned g_linear_status;
+
+__global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass a, int nst) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int nin = a.nin;
+  const int stage_bytes = nin * kLSeg;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes);
+  uint64_t* empty = full + nst;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      pipe::bar_init(full + s, 1);
+      pipe::bar_init(empty + s, kLLanes);
+    }
+    pipe::bar_init_fence();
+  }
+  __syncthreads();
+  const int64_t vend = a.begin + (((a.end - a.begin) >> 4) << 4);  // end of the whole-vector part
+  const int64_t items = (vend - a.begin + kLSeg - 1) / kLSeg;
+
+  if (threadIdx.x >= kLLanes) {  // producer warp
+    if (threadIdx.x != kLLanes) return;
+    pipe::Ring r;
+    int64_t filled = 0;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+      if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
+        atomicOr(&g_linear_status, 1u);
+        pipe::producer_drain(full, nst, r, filled);
+        return;
+      }
+      const int64_t off = a.begin + it * kLSeg;
+      const int64_t bytes = vend - off < kLSeg ? vend - off : kLSeg;
+      pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * nin));
+      unsigned char* dst = smem + (size_t)r.stage * stage_bytes;
+      for (int i = 0; i < nin; ++i) {
+        unsigned char* d = dst + i * kLSeg;
+        if (off + bytes <= a.split) {
+          pipe::bulk_load(d, a.in_lo[i] + off, (uint32_t)bytes, full + r.stage);
+        } else if (off >= a.split) {
+          pipe::bulk_load(d, a.in_hi[i] + (off - a.split), (uint32_t)bytes, full + r.stage);
+        } else {
+          const uint32_t b0 = (uint32_t)(a.split - off);
+          pipe::bulk_load(d, a.in_lo[i] + off, b0, full + r.stage);
+          pipe::bulk_load(d + b0, a.in_hi[i], (uint32_t)bytes - b0, full + r.stage);
+        }
+      }
+      r.next(nst);
+      ++filled;
+    }
+    return;
+  }
+
+  const int lane = threadIdx.x;
+  pipe::Ring r;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    if (!pipe::bar_wait(full + r.stage, r.phase)) {
+      atomicOr(&g_linear_status, 2u);
+      return;
+    }
+    const int64_t off = a.begin + it * kLSeg + lane * 16;
+    const uint4* st = reinterpret_cast<const uint4*>(smem + (size_t)r.stage * stage_bytes) + lane;
+    uint4 acc = vzero();
+    if (off < vend)
+      for (int i = 0; i < nin; ++i) acc = vxor(acc, st[i * kLLanes]);
+    pipe::bar_arrive(empty + r.stage);
+    r.next(nst);
+    if (off < vend)
+      for (int o = 0; o < a.nout; ++o)
+        if (off + 16 <= a.out_end[o]) st16(seg(a.out_lo[o], a.out_hi[o], a.split, off), acc);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, vend);
+}
+
+// ------------------------------------------------- GF(2^8), fixed input count
+// NIN a compile-time constant: every input's 16-byte vector is loaded before
+// any lookup, table offsets are immediates, and the packed table words (byte j
+// of an entry = output j's product) are XORed across inputs per data byte
+// position; one 4x4 byte transpose per word then yields every output word.
+// Tables: 256 u32 entries per input, replicated R times (lane l reads copy
+// l % R); built once per CTA into a compact array, then fanned out with
+// consecutive threads writing consecutive words (no bank conflicts).
+template <int NIN>
+__global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
+  constexpr int R = NIN <= 6 ? 32 : 16;
+  constexpr int RSH = R == 32 ? 5 : 4;
+  extern __shared__ __align__(128) uint32_t tab[];   // [NIN][256][R]
+  uint32_t* compact = tab + NIN * 256 * R;           // [NIN][256]
+  for (int e = threadIdx.x; e < NIN * 256; e += blockDim.x) {
+    const int i = e >> 8, x = e & 255;
+    uint32_t entry = 0;
+    for (int j = 0; j < a.nout; ++j) entry |= gf8_mul((uint32_t)(a.coef[j][i] & 0xffu), (uint32_t)x) << (8 * j);
+    compact[e] = entry;
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < NIN * 256 * R; w += blockDim.x) tab[w] = compact[w >> RSH];
+  __syncthreads();
+
+  const uint32_t lane_off = (threadIdx.x & (R - 1));
+  const char* in_lo[NIN];
+  const char* in_hi[NIN];
+#pragma unroll
+  for (int i = 0; i < NIN; ++i) {
+    in_lo[i] = a.in_lo[i];
+    in_hi[i] = a.in_hi[i];
+  }
   const int64_t nvec = (a.end - a.begin) >> 4;
-  const int64_t step = (int64_t)gridDim.x * blockDim.x * VPT;
-  for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x * VPT + threadIdx.x; v0 < nvec; v0 += step) {
-    uint4 acc[VPT];
-    int64_t off[VPT];
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
+    const int64_t off = a.begin + (v << 4);
+    uint4 x[NIN];
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      acc[j] = vzero();
-      off[j] = a.begin + ((v0 + (int64_t)j * blockDim.x) << 4);
-    }
-#pragma unroll 4
-    for (int i = 0; i < a.nin; ++i) {
-      const char* lo = a.in_lo[i];
-      const char* hi = a.in_hi[i];
+    for (int i = 0; i < NIN; ++i) x[i] = ld16(seg(in_lo[i], in_hi[i], a.split, off));
+    uint32_t acc[4][4];  // [word][byte position]
 #pragma unroll
-      for (int j = 0; j < VPT; ++j)
-        if (v0 + (int64_t)j * blockDim.x < nvec) acc[j] = vxor(acc[j], ld16(seg(lo, hi, a.split, off[j])));
-    }
-    for (int o = 0; o < a.nout; ++o) {
+    for (int w = 0; w < 4; ++w)
 #pragma unroll
-      for (int j = 0; j < VPT; ++j)
-        if (v0 + (int64_t)j * blockDim.x < nvec && off[j] + 16 <= a.out_end[o])
-          st16(seg(a.out_lo[o], a.out_hi[o], a.split, off[j]), acc[j]);
+      for (int b = 0; b < 4; ++b) acc[w][b] = 0u;
+#pragma unroll
+    for (int i = 0; i < NIN; ++i) {
+      const uint32_t* t = tab + i * 256 * R + lane_off;
+      const uint32_t xs[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t d = xs[w];
+        acc[w][0] ^= t[(d & 0xffu) << RSH];
+        acc[w][1] ^= t[((d >> 8) & 0xffu) << RSH];
+        acc[w][2] ^= t[((d >> 16) & 0xffu) << RSH];
+        acc[w][3] ^= t[(d >> 24) << RSH];
+      }
     }
+    uint32_t o[4][4];  // [output][word]
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t u = __byte_perm(acc[w][0], acc[w][1], 0x5140);
+      const uint32_t q = __byte_perm(acc[w][2], acc[w][3], 0x5140);
+      const uint32_t u2 = __byte_perm(acc[w][0], acc[w][1], 0x7362);
+      const uint32_t q2 = __byte_perm(acc[w][2], acc[w][3], 0x7362);
+      o[0][w] = __byte_perm(u, q, 0x5410);
+      o[1][w] = __byte_perm(u, q, 0x7632);
+      o[2][w] = __byte_perm(u2, q2, 0x5410);
+      o[3][w] = __byte_perm(u2, q2, 0x7632);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < a.nout && off + 16 <= a.out_end[j])
+        st16(seg(a.out_lo[j], a.out_hi[j], a.split, off), make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]));
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
 }
@@ -241,8 +365,8 @@ bool pass_aligned(const LinearPass& a) {
 
 template <typename K>
 int occupancy_grid(K kernel, int threads, size_t smem, int64_t work_items) {
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  static LaunchCache cache;  // one per kernel instantiation
+  int per_sm = cache.blocks_per_sm(kernel, threads, smem);
   if (per_sm < 1) per_sm = 1;
   int64_t grid = (int64_t)sm_count() * per_sm;
   const int64_t need = (work_items + threads - 1) / threads;
@@ -261,8 +385,6 @@ template <int NOUT, int R>
 int launch_gf8(const LinearPass& a, cudaStream_t s) {
   const size_t smem = (size_t)a.nin * 256 * 4 * R;
   auto k = gf8_vec_kernel<NOUT, R>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return check_launch("gf8 smem attribute");
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
   k<<<grid, threads, smem, s>>>(a);
@@ -273,12 +395,21 @@ template <int NOUT, int R>
 int launch_gf16(const LinearPass& a, cudaStream_t s) {
   const size_t smem = (size_t)a.nin * 512 * 4 * R;
   auto k = gf16_vec_kernel<NOUT, R>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return check_launch("gf16 smem attribute");
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
   k<<<grid, threads, smem, s>>>(a);
   return check_launch("gf16_vec_kernel");
+}
+
+template <int NIN>
+int launch_gf8_fixed(const LinearPass& a, cudaStream_t s) {
+  constexpr int R = NIN <= 6 ? 32 : 16;
+  const size_t smem = (size_t)NIN * 256 * 4 * (R + 1);
+  auto k = gf8_fixed_kernel<NIN>;
+  const int threads = 1024;
+  const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
+  k<<<grid, threads, smem, s>>>(a);
+  return check_launch("gf8_fixed_kernel");
 }
 
 template <int NOUT>
@@ -308,6 +439,16 @@ constexpr int64_t kTableBudget = 192 * 1024;
 
 }  // namespace
 
+unsigned linear_device_status(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_linear_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_linear_status, &z, sizeof(z));
+  }
+  return v;
+}
+
 int run_linear(const LinearPass& a, cudaStream_t s) {
   if (a.end <= a.begin || a.nout == 0) return GSEC_OK;
   if (a.nin < 1 || a.nin > kLinMaxIn || a.nout < 0 || a.nout > kLinMaxOut) {
@@ -323,13 +464,30 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
   }
   switch (a.field) {
     case Field::XOR: {
-      constexpr int VPT = 4;
-      const int threads = 256;
-      const int grid = occupancy_grid(xor_vec_kernel<VPT>, threads, 0, ((a.end - a.begin) >> 4) / VPT + 1);
-      xor_vec_kernel<VPT><<<grid, threads, 0, s>>>(a);
-      return check_launch("xor_vec_kernel");
+      static LaunchCache cache;
+      const size_t smem = (size_t)kLStages * a.nin * kLSeg + 2 * kLStages * sizeof(uint64_t);
+      int per_sm = cache.blocks_per_sm(xor_tma_kernel, kLLanes + 32, smem);
+      if (per_sm < 0) return check_launch("xor_tma launch shape");
+      per_sm = per_sm > 5 ? 5 : per_sm;
+      const int64_t items = ((a.end - a.begin) / 16 * 16 + kLSeg - 1) / kLSeg;
+      int64_t grid = (int64_t)sm_count() * per_sm;
+      if (grid > items) grid = items;
+      if (grid < 1) grid = 1;
+      xor_tma_kernel<<<(int)grid, kLLanes + 32, smem, s>>>(a, kLStages);
+      return check_launch("xor_tma_kernel");
     }
     case Field::GF8: {
+      switch (a.nin) {
+        case 1: return launch_gf8_fixed<1>(a, s);
+        case 2: return launch_gf8_fixed<2>(a, s);
+        case 3: return launch_gf8_fixed<3>(a, s);
+        case 4: return launch_gf8_fixed<4>(a, s);
+        case 5: return launch_gf8_fixed<5>(a, s);
+        case 6: return launch_gf8_fixed<6>(a, s);
+        case 7: return launch_gf8_fixed<7>(a, s);
+        case 8: return launch_gf8_fixed<8>(a, s);
+        default: break;
+      }
       const int r = pick_replicas((int64_t)a.nin * 256 * 4, kTableBudget);
       switch (a.nout) {
         case 1: return dispatch_gf8<1>(a, r, s);

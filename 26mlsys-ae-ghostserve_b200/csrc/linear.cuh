@@ -32,6 +32,9 @@ struct LinearPass {
   Field field;
 };
 
+// Device status word of the staged linear kernels (non-zero: a bounded wait gave up).
+unsigned linear_device_status(bool clear);
+
 // Launch one pass on `stream` (chooses vector or scalar kernels by alignment).
 int run_linear(const LinearPass& pass, cudaStream_t stream);
 

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "pipe.cuh"
 #include "rdp.cuh"
 
 namespace gsec {
@@ -84,6 +85,110 @@ __global__ void __launch_bounds__(256) rdp_encode_kernel(const RdpEncodeArgs a) 
   }
 }
 
+// ------------------------------------------------------- encode (TMA ring) --
+// Same arithmetic as rdp_encode_kernel, with the data cells staged in shared
+// memory by bulk copies.  Work item = (stripe, 1 KiB segment of the unit);
+// one ring stage = row r of the item's k data cells (k x 1 KiB).  64 consumer
+// threads own 16-byte lanes of the segment; a 32-thread producer warp (one
+// active lane) keeps kStages rows in flight.
+constexpr int kSeg = 1024;
+constexpr int kSegLanes = kSeg / 16;
+static __device__ unsigned g_rdp_status;
+
+template <int P>
+__global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const RdpEncodeArgs a, int nst) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int k = a.k;
+  const int stage_bytes = k * kSeg;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes);
+  uint64_t* empty = full + nst;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      pipe::bar_init(full + s, 1);
+      pipe::bar_init(empty + s, kSegLanes);
+    }
+    pipe::bar_init_fence();
+  }
+  __syncthreads();
+  const int64_t spu = a.unit / kSeg;
+  const int64_t items = (a.s_end - a.s_begin) * spu;
+  const int64_t sb = (int64_t)(P - 1) * a.unit;
+
+  if (threadIdx.x >= kSegLanes) {  // producer warp
+    if (threadIdx.x != kSegLanes) return;
+    pipe::Ring r;
+    int64_t filled = 0;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+      const int64_t stripe = a.s_begin + it / spu;
+      const int64_t seg0 = (it % spu) * kSeg;
+      for (int row = 0; row < P - 1; ++row) {
+        if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
+          atomicOr(&g_rdp_status, 1u);
+          pipe::producer_drain(full, nst, r, filled);
+          return;
+        }
+        const int64_t off = stripe * sb + (int64_t)row * a.unit + seg0;
+        int64_t bytes = a.data_bytes - off;
+        bytes = bytes < 0 ? 0 : (bytes > kSeg ? kSeg : bytes);
+        pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * k));
+        unsigned char* dst = smem + (size_t)r.stage * stage_bytes;
+        if (bytes > 0) {
+          for (int c = 0; c < k; ++c) {
+            unsigned char* d = dst + c * kSeg;
+            if (off + bytes <= a.split) {
+              pipe::bulk_load(d, a.d_lo[c] + off, (uint32_t)bytes, full + r.stage);
+            } else if (off >= a.split) {
+              pipe::bulk_load(d, a.d_hi[c] + (off - a.split), (uint32_t)bytes, full + r.stage);
+            } else {  // the K|V boundary falls inside this segment
+              const uint32_t b0 = (uint32_t)(a.split - off);
+              pipe::bulk_load(d, a.d_lo[c] + off, b0, full + r.stage);
+              pipe::bulk_load(d + b0, a.d_hi[c], (uint32_t)bytes - b0, full + r.stage);
+            }
+          }
+        }
+        r.next(nst);
+        ++filled;
+      }
+    }
+    return;
+  }
+
+  const int lane = threadIdx.x;
+  pipe::Ring r;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t stripe = a.s_begin + it / spu;
+    const int64_t base = stripe * sb + (it % spu) * kSeg + lane * 16;
+    uint4 q[P];
+#pragma unroll
+    for (int d = 0; d < P; ++d) q[d] = vzero();
+#pragma unroll
+    for (int row = 0; row < P - 1; ++row) {
+      if (!pipe::bar_wait(full + r.stage, r.phase)) {
+        atomicOr(&g_rdp_status, 2u);
+        return;
+      }
+      const int64_t off = base + (int64_t)row * a.unit;
+      const uint4* st = reinterpret_cast<const uint4*>(smem + (size_t)r.stage * stage_bytes) + lane;
+      const bool in_data = off < a.data_bytes;
+      uint4 prow = vzero();
+#pragma unroll
+      for (int c = 0; c < P - 1; ++c) {
+        if (c < k && in_data) {
+          const uint4 x = st[c * kSegLanes];
+          prow = vxor(prow, x);
+          if ((row + c) % P != P - 1) q[(row + c) % P] = vxor(q[(row + c) % P], x);
+        }
+      }
+      pipe::bar_arrive(empty + r.stage);
+      r.next(nst);
+      st16(a.parity[0] + off, prow);
+      if ((row + P - 1) % P != P - 1) q[(row + P - 1) % P] = vxor(q[(row + P - 1) % P], prow);
+    }
+#pragma unroll
+    for (int d = 0; d < P - 1; ++d) st16(a.parity[1] + base + (int64_t)d * a.unit, q[d]);
+  }
+}
+
 // ---------------------------------------------------------------- decode ----
 template <int P>
 __global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) {
@@ -135,8 +240,8 @@ __global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) 
 
 template <typename K>
 int grid_for(K kernel, int threads, int64_t items) {
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+  static LaunchCache cache;
+  int per_sm = cache.blocks_per_sm(kernel, threads, 0);
   if (per_sm < 1) per_sm = 1;
   int64_t grid = (int64_t)sm_count() * per_sm;
   const int64_t need = (items + threads - 1) / threads;
@@ -144,8 +249,24 @@ int grid_for(K kernel, int threads, int64_t items) {
   return (int)(grid < 1 ? 1 : grid);
 }
 
+constexpr int kStages = 3;
+constexpr int kCtasPerSm = 5;
+
 template <int P>
 int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
+  if (a.unit % kSeg == 0) {  // TMA ring: units split into whole 1 KiB segments
+    static LaunchCache cache;
+    auto k = rdp_encode_tma_kernel<P>;
+    const size_t smem = (size_t)kStages * a.k * kSeg + 2 * kStages * sizeof(uint64_t);
+    int per_sm = cache.blocks_per_sm(k, kSegLanes + 32, smem);
+    if (per_sm < 0) return check_launch("rdp_encode_tma launch shape");
+    per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
+    const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
+    int64_t grid = (int64_t)sm_count() * per_sm;
+    if (grid > items) grid = items;
+    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, kStages);
+    return check_launch("rdp_encode_tma_kernel");
+  }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
   const int threads = 256;
   const int grid = grid_for(rdp_encode_kernel<P>, threads, items);
@@ -162,6 +283,16 @@ int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+unsigned rdp_device_status(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_rdp_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_rdp_status, &z, sizeof(z));
+  }
+  return v;
+}
 
 bool rdp_prime_supported(int p) {
   return p == 3 || p == 5 || p == 7 || p == 11 || p == 13 || p == 17;

@@ -36,6 +36,8 @@ struct RdpDecodeArgs {
 };
 
 bool rdp_prime_supported(int p);
+// Device status word of the RDP kernels (non-zero: a bounded wait gave up).
+unsigned rdp_device_status(bool clear);
 int rdp_encode(const RdpEncodeArgs& a, cudaStream_t s);
 int rdp_decode(const RdpDecodeArgs& a, cudaStream_t s);
 int rdp_solve_masks(int p, const int* cols, int ncols, uint32_t mask[2][16]);

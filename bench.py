@@ -232,6 +232,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--verify", action="store_true", help="check every rank's parity against a local re-encode")
+    ap.add_argument("--op", default="encode", choices=["encode", "decode"],
+                    help="decode: rebuild data shards 0 and 1 (2 erasures) each step instead of encoding")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -275,8 +278,16 @@ def main():
     stream = torch.cuda.current_stream()
     sh = int(stream.cuda_stream)
 
-    def step():
-        g.codec.encode_ptrs(spec, data_ptrs, None, nbytes, nbytes, par_ptrs, 0, pbytes, sh)
+    step = g.codec.PreparedEncode(spec, data_ptrs, None, nbytes, nbytes, par_ptrs, 0, pbytes, sh)
+    if args.op == "decode":
+        step()  # the parity the decode reads
+        torch.cuda.synchronize()
+        erased = list(range(min(m, k)))  # data shards 0..m-1 lost: the heaviest pattern
+        rebuilt = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in erased]
+        shard_ptrs = list(data_ptrs) + par_ptrs
+        for e, t in zip(erased, rebuilt):
+            shard_ptrs[e] = t.data_ptr()
+        step = g.codec.PreparedDecode(spec, shard_ptrs, None, nbytes, nbytes, erased, 0, pbytes, sh)
 
     def barrier():
         if world > 1:
@@ -304,17 +315,32 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     barrier()
+    verified = None
+    if args.verify and args.op == "decode":
+        torch.cuda.synchronize()
+        ok = all(torch.equal(t, slots[e]) for e, t in zip(erased, rebuilt)) if world == 1 else True
+        verified = ok and g.codec.device_status(clear=True) == 0
+    elif args.verify:
+        verified = verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device)
+        if world > 1:
+            t = torch.tensor([0 if verified else 1], device=device)
+            dist.all_reduce(t)
+            verified = int(t.item()) == 0
     ms_step = ms / args.steps
     per_gpu = alg_bytes / (ms_step * 1e-3) / 1e9
     value = per_gpu * world
 
     peak, peak_kind = load_peaks()
     tag = {"rdp": "rdp_encode_p7_config1", "rs8": "rs8_encode_6_2_config2", "xor": "xor_encode_7_config0"}[wl["scheme"]]
+    if args.op == "decode":
+        tag = tag.replace("encode", "decode")
     roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu / peak, 4), "traffic": traffic_from_profiles(tag),
                 "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
-                "kernel": {"rdp": "rdp_encode_kernel<7>", "rs8": "gf8_vec_kernel<2,32>",
-                           "xor": "xor_vec_kernel<4>"}[wl["scheme"]]}
+                "kernel": ({"rdp": "rdp_encode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
+                           if args.op == "encode" else
+                           {"rdp": "rdp_decode_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
+                           )[wl["scheme"]]}
     if world > 1:
         link = 770.0
         t_roof = max((alg_bytes - remote_bytes) / (peak * 1e9), remote_bytes / (link * 1e9))
@@ -323,11 +349,11 @@ def main():
                               "roof_ms": round(t_roof * 1e3, 4), "frac_of_roof": round(t_roof * 1e3 / ms_step, 4)}
 
     e2e = None
-    if not args.no_e2e and world == 1:
+    if not args.no_e2e and world == 1 and args.op == "encode":
         e2e = measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, max(3, min(args.steps, 20)))
 
     cpu_baseline = None
-    if not args.no_cpu_baseline and rank == 0 and world == 1:
+    if not args.no_cpu_baseline and rank == 0 and world == 1 and args.op == "encode":
         host = [t.cpu().numpy() for t in slots]
         rate, reps, threads, el = cpu_encode_rate(wl, host, args.cpu_seconds)
         cpu_baseline = {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -338,7 +364,7 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": wl["desc"], "k": k, "m": m, "p": wl["p"],
+            "config": {"workload": args.workload, "op": args.op, "desc": wl["desc"], "k": k, "m": m, "p": wl["p"],
                        "unit": wl["unit"], "shard_bytes": nbytes, "parity_bytes": pbytes,
                        "per_gpu_gbs": round(per_gpu, 2),
                        "l2": f"working set {(alg_bytes) / MIB:.0f} MiB per step > 126 MB L2, no flush",
@@ -346,11 +372,26 @@ def main():
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
             "gpu_launches": args.steps, "clocks": clocks,
         }
+        if verified is not None:
+            line["verified"] = verified
         print(json.dumps(line), flush=True)
     if peer_group is not None:
         peer_group.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device):
+    """Copy this rank's codeword shards (local or peer) into local buffers, encode
+    them again and compare with the parity the timed loop produced."""
+    L = g._lib
+    local = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in data_ptrs]
+    for dst, src in zip(local, data_ptrs):  # gsec_rows_pack as a copy kernel (reads peer memory)
+        L.call("gsec_rows_pack", L.C.c_void_p(src), nbytes, None, 0, L.C.c_void_p(dst.data_ptr()), nbytes, nbytes, 1,
+               L.C.c_void_p(g.codec.stream_handle()))
+    again = g.encode(spec, local)
+    torch.cuda.synchronize()
+    return all(torch.equal(a, b) for a, b in zip(again, parity)) and g.codec.device_status(clear=True) == 0
 
 
 def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):

@@ -65,6 +65,13 @@ typedef struct gsec_code {
 GSEC_API const char* gsec_last_error(void);
 /* Library version string. */
 GSEC_API const char* gsec_version(void);
+/* Device status of the current GPU (synchronous: waits for this device's
+ * pending work). Kernels that stage data through TMA bulk copies bound every
+ * wait; one that gives up sets a bit here and returns early, so a non-zero
+ * status means some call since the last clear produced incomplete output.
+ * clear != 0 resets it. No counterpart in the reference (its kernels have no
+ * waits). */
+GSEC_API int gsec_device_status(uint32_t* status, int32_t clear);
 
 /* ------------------------------------------------------------------------- */
 /* Engine: position-sliced encode / decode over per-shard pointers            */

@@ -13,10 +13,17 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 
-def _init(rank, world, port):
+def _init(rank, world, port, backend="gloo"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    if backend == "nccl":
+        import datetime
+
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
 
 
 def _pkg(sub=""):
@@ -120,14 +127,16 @@ def ipc_sliced_encode(rank, world, port, scheme, out):
     dist.destroy_process_group()
 
 
-def hook_fused(rank, world, port, out):
-    """The hook's fused mode end to end on 2 processes sharing one GPU."""
-    _init(rank, world, port)
-    torch.cuda.set_device(0)
+def hook_fused(rank, world, port, backend, unit, out):
+    """The hook's fused mode end to end: gloo = ranks sharing cuda:0 (CUDA IPC
+    within one device), nccl = one GPU per rank (NVLink peer reads)."""
+    _init(rank, world, port, backend)
+    dev = rank if backend == "nccl" else 0
+    torch.cuda.set_device(dev)
     hook = _pkg("hook")
     from oracle import codes
 
-    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme="rdp", unit=512, metrics_file=None))
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme="rdp", unit=unit, metrics_file=None))
     rng = np.random.default_rng(7 + rank)
     ok = True
     for step in range(3):
@@ -136,14 +145,14 @@ def hook_fused(rank, world, port, out):
         v = torch.from_numpy(rng.standard_normal((tokens, 1, 128)).astype(np.float32)).cuda().to(torch.bfloat16)
         par, (lo, hi) = ft.encode_chunk(k, v, step + 1)
         torch.cuda.synchronize()
-        shard = torch.cat([k.view(torch.uint8).reshape(-1), v.view(torch.uint8).reshape(-1)]).cpu()
-        shards = [torch.empty_like(shard) for _ in range(world)]
-        dist.all_gather(shards, shard)
+        shard = torch.cat([k.view(torch.uint8).reshape(-1), v.view(torch.uint8).reshape(-1)]).cpu().numpy()
+        shards = [None] * world
+        dist.all_gather_object(shards, shard)
         got = [None] * world
         dist.all_gather_object(got, [p.cpu().numpy() for p in par])
         if rank == 0:
             spec = ft._spec(world)
-            want = codes.rdp_encode([s.numpy() for s in shards], spec.p, spec.unit)
+            want = codes.rdp_encode(list(shards), spec.p, spec.unit)
             for j in range(2):
                 ok = ok and np.array_equal(np.concatenate([got[r][j] for r in range(world)]), want[j])
     ft.close()

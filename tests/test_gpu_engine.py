@@ -17,6 +17,13 @@ from oracle import codes
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def device_status_clean():
+    """Every staged kernel's bounded waits completed (libgsec status word 0)."""
+    yield
+    assert pkg("codec").device_status(clear=True) == 0
+
+
 def dev(a: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
@@ -113,12 +120,14 @@ def test_rs8_matches_oracle_every_pattern(rng, k, m):
 
 
 # ---------------------------------------------------- segments and ranges ----
-@pytest.mark.parametrize("scheme", ["xor", "rdp", "rs8"])
+@pytest.mark.parametrize("scheme", ["xor", "rdp", "rdp4k", "rs8"])
 def test_two_segment_shards_equal_concatenation(rng, scheme):
     g = pkg()
     k = 6
-    spec = {"xor": g.CodeSpec.xor(k), "rdp": g.CodeSpec.rdp(k, 7, 256), "rs8": g.CodeSpec.rs8(k, 2)}[scheme]
-    lo_b, hi_b = 16 * 301, 16 * 257
+    spec = {"xor": g.CodeSpec.xor(k), "rdp": g.CodeSpec.rdp(k, 7, 256), "rs8": g.CodeSpec.rs8(k, 2),
+            "rdp4k": g.CodeSpec.rdp(k, 7, 4096)}[scheme]
+    # the split falls inside a 1 KiB staging segment (TMA kernels copy it in two parts)
+    lo_b, hi_b = (16 * 301, 16 * 257) if scheme != "rdp4k" else (6 * 4096 + 16 * 301, 6 * 4096 + 16 * 257)
     lo = [rand_bytes(rng, lo_b) for _ in range(k)]
     hi = [rand_bytes(rng, hi_b) for _ in range(k)]
     cat = [dev(np.concatenate([a, b])) for a, b in zip(lo, hi)]

@@ -1,0 +1,21 @@
+"""Fused P2P path on real multi-GPU: one process per GPU, NCCL for control,
+NVLink peer reads inside the encode kernel. Skipped with fewer than 2 GPUs."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import mp_workers
+from test_hook import run_ranks
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+@pytest.mark.parametrize("unit", [512, 4096])
+def test_hook_fused_mode_two_gpus(unit):
+    res = run_ranks(mp_workers.hook_fused, 2, "nccl", unit, timeout=300)
+    assert res[0][1] is True
+    for _rank, _ok, recs in res:
+        assert recs == [1, 2, 3]

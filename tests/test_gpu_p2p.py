@@ -18,8 +18,9 @@ def test_ipc_sliced_encode_two_ranks(scheme):
     assert res[0][1] is True
 
 
-def test_hook_fused_mode_two_ranks():
-    res = run_ranks(mp_workers.hook_fused, 2, timeout=300)
+@pytest.mark.parametrize("unit", [512, 4096])
+def test_hook_fused_mode_two_ranks(unit):
+    res = run_ranks(mp_workers.hook_fused, 2, "gloo", unit, timeout=300)
     assert res[0][1] is True
     for _rank, _ok, recs in res:
         assert recs == [1, 2, 3]
