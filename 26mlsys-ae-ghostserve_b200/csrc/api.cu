@@ -46,6 +46,11 @@ int current_device() {
   return cudaGetDevice(&dev) == cudaSuccess ? dev : -1;
 }
 
+LaunchCache& launch_cache() {
+  static LaunchCache cache;
+  return cache;
+}
+
 int sm_count() {
   static int cache[64] = {0};
   int dev = 0;

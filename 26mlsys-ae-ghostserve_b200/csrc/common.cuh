@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -37,43 +38,55 @@ int sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Per-device cache of a kernel's launch shape: the dynamic shared memory
-// attribute is raised once and resident-CTA counts are queried once per
-// shared-memory size, instead of on every launch.
+// Per-device cache of kernels' launch shapes: a kernel's dynamic shared
+// memory attribute is raised once and its resident-CTA count is queried once
+// per (device, kernel, shared-memory size), instead of on every launch.
 int current_device();
 
-struct LaunchCache {
-  static constexpr int kDevices = 64;
-  static constexpr int kSlots = 8;
-  size_t attr_smem[kDevices] = {};
-  size_t smem[kDevices][kSlots] = {};
-  int per_sm[kDevices][kSlots] = {};
-  std::mutex mu;
-
+class LaunchCache {
+ public:
   template <typename K>
   int blocks_per_sm(K kernel, int threads, size_t dyn_smem) {
-    std::lock_guard<std::mutex> lock(mu);
+    const void* fn = reinterpret_cast<const void*>(kernel);
+    std::lock_guard<std::mutex> lock(mu_);
     const int dev = current_device();
-    if (dev < 0 || dev >= kDevices) return -1;
-    if (dyn_smem > attr_smem[dev]) {
+    if (dev < 0) return -1;
+    size_t& attr = attr_[{dev, fn}];
+    if (dyn_smem > attr) {
       if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem) != cudaSuccess)
         return -1;
-      attr_smem[dev] = dyn_smem;
+      attr = dyn_smem;
     }
-    for (int i = 0; i < kSlots; ++i)
-      if (per_sm[dev][i] > 0 && smem[dev][i] == dyn_smem) return per_sm[dev][i];
+    const Key key{dev, fn, dyn_smem, threads};
+    auto it = per_sm_.find(key);
+    if (it != per_sm_.end()) return it->second;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, dyn_smem) != cudaSuccess) return -1;
     if (n < 1) n = 1;
-    for (int i = 0; i < kSlots; ++i)
-      if (per_sm[dev][i] == 0) {
-        smem[dev][i] = dyn_smem;
-        per_sm[dev][i] = n;
-        break;
-      }
+    per_sm_[key] = n;
     return n;
   }
+
+ private:
+  struct Key {
+    int dev;
+    const void* fn;
+    size_t smem;
+    int threads;
+    bool operator<(const Key& o) const {
+      if (dev != o.dev) return dev < o.dev;
+      if (fn != o.fn) return fn < o.fn;
+      if (smem != o.smem) return smem < o.smem;
+      return threads < o.threads;
+    }
+  };
+  std::mutex mu_;
+  std::map<std::pair<int, const void*>, size_t> attr_;
+  std::map<Key, int> per_sm_;
 };
+
+// The process-wide cache.
+LaunchCache& launch_cache();
 
 // ---------------------------------------------------------- vector access ---
 

@@ -171,7 +171,13 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
   for (int w = threadIdx.x; w < NIN * 256 * R; w += blockDim.x) tab[w] = compact[w >> RSH];
   __syncthreads();
 
-  const uint32_t lane_off = (threadIdx.x & (R - 1));
+  // Byte offset of this lane's replica inside an entry; entries are R*4 bytes
+  // apart, so (data byte << log2(R*4)) | lane_off addresses a lookup with one
+  // shift and one LOP3, the table's base being an immediate per input.
+  constexpr int ESH = RSH + 2;
+  constexpr uint32_t EMASK = 0xffu << ESH;
+  const uint32_t lane_off = (threadIdx.x & (R - 1)) * 4u;
+  const unsigned char* tb = reinterpret_cast<const unsigned char*>(tab);
   const char* in_lo[NIN];
   const char* in_hi[NIN];
 #pragma unroll
@@ -193,15 +199,15 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
       for (int b = 0; b < 4; ++b) acc[w][b] = 0u;
 #pragma unroll
     for (int i = 0; i < NIN; ++i) {
-      const uint32_t* t = tab + i * 256 * R + lane_off;
+      const unsigned char* t = tb + i * 256 * R * 4;
       const uint32_t xs[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const uint32_t d = xs[w];
-        acc[w][0] ^= t[(d & 0xffu) << RSH];
-        acc[w][1] ^= t[((d >> 8) & 0xffu) << RSH];
-        acc[w][2] ^= t[((d >> 16) & 0xffu) << RSH];
-        acc[w][3] ^= t[(d >> 24) << RSH];
+        acc[w][0] ^= *reinterpret_cast<const uint32_t*>(t + (((d << ESH) & EMASK) | lane_off));
+        acc[w][1] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (8 - ESH)) & EMASK) | lane_off));
+        acc[w][2] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (16 - ESH)) & EMASK) | lane_off));
+        acc[w][3] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (24 - ESH)) & EMASK) | lane_off));
       }
     }
     uint32_t o[4][4];  // [output][word]
@@ -365,7 +371,7 @@ bool pass_aligned(const LinearPass& a) {
 
 template <typename K>
 int occupancy_grid(K kernel, int threads, size_t smem, int64_t work_items) {
-  static LaunchCache cache;  // one per kernel instantiation
+  LaunchCache& cache = launch_cache();
   int per_sm = cache.blocks_per_sm(kernel, threads, smem);
   if (per_sm < 1) per_sm = 1;
   int64_t grid = (int64_t)sm_count() * per_sm;
@@ -464,7 +470,7 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
   }
   switch (a.field) {
     case Field::XOR: {
-      static LaunchCache cache;
+      LaunchCache& cache = launch_cache();
       const size_t smem = (size_t)kLStages * a.nin * kLSeg + 2 * kLStages * sizeof(uint64_t);
       int per_sm = cache.blocks_per_sm(xor_tma_kernel, kLLanes + 32, smem);
       if (per_sm < 0) return check_launch("xor_tma launch shape");

@@ -238,9 +238,128 @@ __global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) 
   }
 }
 
+// ------------------------------------------------------- decode (TMA ring) --
+// rdp_decode_kernel's syndrome decode with the surviving cells staged in shared
+// memory: one ring stage = row r of every surviving column of the item
+// (stripe, 1 KiB segment), packed in column order.
+template <int P>
+__global__ void __launch_bounds__(kSegLanes + 32) rdp_decode_tma_kernel(const RdpDecodeArgs a, int nst) {
+  constexpr int NS = 2 * (P - 1);
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int nalive = __popc(a.alive);
+  const int stage_bytes = nalive * kSeg;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes);
+  uint64_t* empty = full + nst;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      pipe::bar_init(full + s, 1);
+      pipe::bar_init(empty + s, kSegLanes);
+    }
+    pipe::bar_init_fence();
+  }
+  __syncthreads();
+  const int64_t spu = a.unit / kSeg;
+  const int64_t items = (a.s_end - a.s_begin) * spu;
+  const int64_t sb = (int64_t)(P - 1) * a.unit;
+
+  if (threadIdx.x >= kSegLanes) {  // producer warp
+    if (threadIdx.x != kSegLanes) return;
+    pipe::Ring r;
+    int64_t filled = 0;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+      const int64_t stripe = a.s_begin + it / spu;
+      const int64_t seg0 = (it % spu) * kSeg;
+      for (int row = 0; row < P - 1; ++row) {
+        if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
+          atomicOr(&g_rdp_status, 4u);
+          pipe::producer_drain(full, nst, r, filled);
+          return;
+        }
+        const int64_t off = stripe * sb + (int64_t)row * a.unit + seg0;
+        int64_t dbytes = a.data_bytes - off;
+        dbytes = dbytes < 0 ? 0 : (dbytes > kSeg ? kSeg : dbytes);
+        uint32_t tx = 0;
+        for (int c = 0; c <= P; ++c)
+          if ((a.alive >> c) & 1u) tx += (uint32_t)(c < P - 1 ? dbytes : kSeg);
+        pipe::bar_expect_tx(full + r.stage, tx);
+        unsigned char* d = smem + (size_t)r.stage * stage_bytes;
+        for (int c = 0; c <= P; ++c) {
+          if (!((a.alive >> c) & 1u)) continue;
+          const int64_t bytes = c < P - 1 ? dbytes : kSeg;
+          if (bytes > 0) {
+            if (off + bytes <= a.split) {
+              pipe::bulk_load(d, a.lo[c] + off, (uint32_t)bytes, full + r.stage);
+            } else if (off >= a.split) {
+              pipe::bulk_load(d, a.hi[c] + (off - a.split), (uint32_t)bytes, full + r.stage);
+            } else {
+              const uint32_t b0 = (uint32_t)(a.split - off);
+              pipe::bulk_load(d, a.lo[c] + off, b0, full + r.stage);
+              pipe::bulk_load(d + b0, a.hi[c], (uint32_t)bytes - b0, full + r.stage);
+            }
+          }
+          d += kSeg;
+        }
+        r.next(nst);
+        ++filled;
+      }
+    }
+    return;
+  }
+
+  const int lane = threadIdx.x;
+  int pos[P + 1];  // slot of column c inside a stage
+#pragma unroll
+  for (int c = 0; c <= P; ++c) pos[c] = __popc(a.alive & ((1u << c) - 1u)) * kSegLanes;
+  pipe::Ring r;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t stripe = a.s_begin + it / spu;
+    const int64_t base = stripe * sb + (it % spu) * kSeg + lane * 16;
+    uint4 syn[NS];
+#pragma unroll
+    for (int j = 0; j < NS; ++j) syn[j] = vzero();
+#pragma unroll
+    for (int row = 0; row < P - 1; ++row) {
+      if (!pipe::bar_wait(full + r.stage, r.phase)) {
+        atomicOr(&g_rdp_status, 8u);
+        return;
+      }
+      const int64_t off = base + (int64_t)row * a.unit;
+      const bool in_data = off < a.data_bytes;
+      const uint4* st = reinterpret_cast<const uint4*>(smem + (size_t)r.stage * stage_bytes) + lane;
+#pragma unroll
+      for (int c = 0; c <= P; ++c) {
+        if (!((a.alive >> c) & 1u)) continue;
+        if (c < P - 1 && !in_data) continue;
+        const uint4 v = st[pos[c]];
+        if (c <= P - 1) {
+          syn[row] = vxor(syn[row], v);
+          if ((row + c) % P != P - 1) syn[(P - 1) + (row + c) % P] = vxor(syn[(P - 1) + (row + c) % P], v);
+        } else {
+          syn[(P - 1) + row] = vxor(syn[(P - 1) + row], v);
+        }
+      }
+      pipe::bar_arrive(empty + r.stage);
+      r.next(nst);
+    }
+    for (int e = 0; e < a.nout; ++e) {
+      const bool out_data = a.out_col[e] < P - 1;
+#pragma unroll
+      for (int row = 0; row < P - 1; ++row) {
+        const int64_t off = base + (int64_t)row * a.unit;
+        const uint32_t m = a.mask[e][row];
+        uint4 o = vzero();
+#pragma unroll
+        for (int j = 0; j < NS; ++j)
+          if ((m >> j) & 1u) o = vxor(o, syn[j]);
+        if (!out_data || off < a.data_bytes) st16(seg(a.out_lo[e], a.out_hi[e], a.split, off), o);
+      }
+    }
+  }
+}
+
 template <typename K>
 int grid_for(K kernel, int threads, int64_t items) {
-  static LaunchCache cache;
+  LaunchCache& cache = launch_cache();
   int per_sm = cache.blocks_per_sm(kernel, threads, 0);
   if (per_sm < 1) per_sm = 1;
   int64_t grid = (int64_t)sm_count() * per_sm;
@@ -255,7 +374,7 @@ constexpr int kCtasPerSm = 5;
 template <int P>
 int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
   if (a.unit % kSeg == 0) {  // TMA ring: units split into whole 1 KiB segments
-    static LaunchCache cache;
+    LaunchCache& cache = launch_cache();
     auto k = rdp_encode_tma_kernel<P>;
     const size_t smem = (size_t)kStages * a.k * kSeg + 2 * kStages * sizeof(uint64_t);
     int per_sm = cache.blocks_per_sm(k, kSegLanes + 32, smem);
@@ -275,6 +394,19 @@ int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
 }
 template <int P>
 int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
+  if (a.unit % kSeg == 0) {
+    LaunchCache& cache = launch_cache();
+    auto k = rdp_decode_tma_kernel<P>;
+    const size_t smem = (size_t)kStages * __builtin_popcount(a.alive) * kSeg + 2 * kStages * sizeof(uint64_t);
+    int per_sm = cache.blocks_per_sm(k, kSegLanes + 32, smem);
+    if (per_sm < 0) return check_launch("rdp_decode_tma launch shape");
+    per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
+    const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
+    int64_t grid = (int64_t)sm_count() * per_sm;
+    if (grid > items) grid = items;
+    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, kStages);
+    return check_launch("rdp_decode_tma_kernel");
+  }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
   const int threads = 256;
   const int grid = grid_for(rdp_decode_kernel<P>, threads, items);
