@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """bench.py — KV parity encode throughput of the B200 erasure-coding engine.
 
-Default workload: textbook RDP with p=7 over 6 data shards
+Default workload (config 1 of the benchmark spec): textbook RDP with p=7 over 6 data shards
 + row parity P + diagonal parity Q, 4 KiB stripe units; each data shard is one
 rank's KV for one 2048-token chunk of a Llama-3.1-8B-architecture model at
 TP=8 (K and V [32 layers, 2048 tokens, 1 kv-head, 128] bf16 ~ N(0,1), seeded):

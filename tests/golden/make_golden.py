@@ -7,7 +7,7 @@ oracle/build_ref.py (oracle/_ref/*) on small seeded inputs generated on the
 host, and writes inputs and outputs to ``ref_*.npz``.  tests/test_golden.py
 checks the CPU oracle (oracle/reference.py) against these files, which pins the
 oracle to the reference's actual behaviour.  Inputs are bf16 N(0,1) bit
-patterns (the KV dtype of the BASELINE configs) handed to the reference as
+patterns (the KV dtype of the benchmark configs) handed to the reference as
 fp16 by bit reinterpretation, plus fp16 N(0,1) for the RS case.
 """
 from __future__ import annotations

@@ -1,7 +1,7 @@
 """GPU parity of the engine codes (XOR, textbook RDP, RS8) against the CPU oracle.
 
 Bit-exact on seeded inputs at small sizes for every erasure pattern; at the
-BASELINE sizes (32 MiB bf16 shards) through size-independent properties:
+benchmark sizes (32 MiB bf16 shards) through size-independent properties:
 encode -> erase every pair -> decode returns the original bytes."""
 from __future__ import annotations
 
@@ -166,7 +166,7 @@ def test_range_slices_compose(rng, scheme):
         assert np.array_equal(a, host(b))
 
 
-# --------------------------------------------------------- BASELINE sizes ----
+# -------------------------------------------------------- benchmark sizes ----
 def kv_shards_bf16(seed: int, k: int):
     """k ranks' KV chunk: K and V [32 layers, 2048 tokens, 1 head, 128] bf16 N(0,1)."""
     gen = torch.Generator(device="cuda").manual_seed(seed)
