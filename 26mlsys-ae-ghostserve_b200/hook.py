@@ -191,20 +191,29 @@ class KVFaultTolerance:
 
     def encode_chunk(self, local_k: torch.Tensor, local_v: torch.Tensor, chunk_id: int):
         """Fused P2P encode of this rank's slice; returns the device parity slices."""
+        return self.encode_parts([local_k], [local_v], chunk_id)
+
+    def encode_parts(self, parts_k, parts_v, chunk_id: int):
+        """Like encode_chunk for a shard made of several tensors (e.g. one chunk's
+        K and V in every layer of a layer-major cache): the parts are copied once,
+        in order, into this rank's peer-mapped staging buffer (K parts, then V
+        parts), and the fused encode reads every rank's staging in place."""
         from . import p2p
 
         rank, world = self._rank_world()
-        device = local_k.device
-        kb = local_k.contiguous().view(torch.uint8).reshape(-1)
-        vb = local_v.contiguous().view(torch.uint8).reshape(-1)
-        half = kb.numel()
-        if half % 16 or vb.numel() != half:
+        device = parts_k[0].device
+        half = sum(t.numel() * t.element_size() for t in parts_k)
+        if half % 16 or sum(t.numel() * t.element_size() for t in parts_v) != half:
             raise ValueError("delta K and V must have equal sizes, multiples of 16 bytes")
         self._ensure_staging(half, device)
         slot = self._calls % 2
         self._calls += 1
-        self._staging[slot][0][:half].copy_(kb)
-        self._staging[slot][1][:half].copy_(vb)
+        for parts, buf in ((parts_k, self._staging[slot][0]), (parts_v, self._staging[slot][1])):
+            dt = parts[0].dtype
+            if all(t.dtype == dt for t in parts):
+                torch.cat([t.reshape(-1) for t in parts], out=buf[:half].view(dt))
+            else:
+                torch.cat([t.reshape(-1).view(torch.uint8) for t in parts], out=buf[:half])
         self._barrier(device)  # every rank's staging write precedes every peer read
         spec = self._spec(world)
         data_bytes = 2 * half

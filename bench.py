@@ -228,7 +228,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill"])
+    ap.add_argument("--prefill-seqs", type=int, default=16)
+    ap.add_argument("--prefill-len", type=int, default=32768)
+    ap.add_argument("--prefill-chunk", type=int, default=2048)
+    ap.add_argument("--prefill-layers", type=int, default=32)
+    ap.add_argument("--parity", default="none,fused,reference",
+                    help="prefill variants to time: none, fused (gsec P2P encode per chunk), reference (the "
+                         "reference hook's gather + parity + host copy per layer)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -236,6 +243,9 @@ def main():
     ap.add_argument("--op", default="encode", choices=["encode", "decode"],
                     help="decode: rebuild data shards 0 and 1 (2 erasures) each step instead of encoding")
     args = ap.parse_args()
+    if args.workload == "prefill":
+        run_prefill_bench(args)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, wl)
@@ -392,6 +402,79 @@ def verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device):
     again = g.encode(spec, local)
     torch.cuda.synchronize()
     return all(torch.equal(a, b) for a, b in zip(again, parity)) and g.codec.device_status(clear=True) == 0
+
+
+def run_prefill_bench(args):
+    """Config 3: TP prefill of a Llama-3.1-8B-architecture model (random bf16
+    weights), prefill tokens/s without parity and with it (fused / reference)."""
+    import datetime
+    import importlib
+    import socket
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if "MASTER_PORT" not in os.environ:
+            sk = socket.socket()
+            sk.bind(("127.0.0.1", 0))
+            os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
+            sk.close()
+        os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    pre = importlib.import_module(PKG + ".prefill")
+    hook = importlib.import_module(PKG + ".hook")
+    spec = pre.ModelSpec(layers=args.prefill_layers)
+    model = pre.TPPrefill(spec, args.prefill_len, device)
+    chunk = args.prefill_chunk
+    variants = [v for v in args.parity.split(",") if v]
+    rates, times = {}, {}
+    for var in variants:
+        ft = None
+        if var != "none":
+            ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused" if var == "fused" else "reference",
+                                                       metrics_file=None))
+        pre.run_prefill(model, 1, min(2 * chunk, args.prefill_len), chunk, var, ft, seed=7)  # warm-up
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tokens = pre.run_prefill(model, args.prefill_seqs, args.prefill_len, chunk, var, ft)
+        if ft is not None:
+            ft.flush()  # the last chunk's parity has reached host memory
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times[var] = float(t.item())
+        rates[var] = tokens / (times[var] * 1e-3)
+        if ft is not None:
+            ft.close()
+    base = rates.get("none")
+    if rank == 0:
+        head = "fused" if "fused" in rates else variants[0]
+        line = {
+            "metric": "prefill tok/s with per-chunk KV parity (Llama-3.1-8B arch, random bf16 weights)",
+            "value": round(rates[head], 1), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
+            "scaling": "strong", "dtype": "bf16", "data": "synthetic (uniform random token ids)",
+            "config": {"workload": "prefill", "tp": world, "seqs": args.prefill_seqs, "seq_len": args.prefill_len,
+                       "chunk": chunk, "layers": args.prefill_layers, "parity_code": "fused: RDP over the TP ranks' "
+                       "per-chunk KV (k = world), reference: mod-S RDP gathered to a rotating rank per layer"},
+            "tok_s": {k: round(v, 1) for k, v in rates.items()},
+            "ms": {k: round(v, 2) for k, v in times.items()},
+            "overhead_pct": {k: round(100.0 * (base / v - 1.0), 2) for k, v in rates.items()
+                             if base and k != "none"},
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):
