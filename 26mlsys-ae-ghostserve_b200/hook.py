@@ -78,6 +78,8 @@ class KVFaultTolerance:
         self._host = []
         self._pending = []        # (record, event, t_enqueue) awaiting D2H completion
         self._copy_stream = None
+        self._parity_free = [None, None]
+        self._ring_next = 0
         self._calls = 0
 
     # ------------------------------------------------------------- control --
@@ -209,11 +211,14 @@ class KVFaultTolerance:
         slot = self._calls % 2
         self._calls += 1
         for parts, buf in ((parts_k, self._staging[slot][0]), (parts_v, self._staging[slot][1])):
-            dt = parts[0].dtype
-            if all(t.dtype == dt for t in parts):
-                torch.cat([t.reshape(-1) for t in parts], out=buf[:half].view(dt))
-            else:
+            if all(t.is_contiguous() for t in parts):
                 torch.cat([t.reshape(-1).view(torch.uint8) for t in parts], out=buf[:half])
+            else:  # strided views: one copy each, straight into the staging buffer
+                off = 0
+                for t in parts:
+                    n = t.numel() * t.element_size()
+                    buf[off:off + n].view(t.dtype).view(t.shape).copy_(t)
+                    off += n
         self._barrier(device)  # every rank's staging write precedes every peer read
         spec = self._spec(world)
         data_bytes = 2 * half
@@ -221,8 +226,15 @@ class KVFaultTolerance:
         g = spec.stripe_bytes()
         lo, hi = p2p.stripe_slice(rank, world, pbytes // g)
         lo, hi = lo * g, hi * g
-        if self._parity is None or self._parity[0].numel() < max(hi - lo, 16):
-            self._parity = [torch.empty(max(hi - lo, 16), dtype=torch.uint8, device=device) for _ in range(spec.m)]
+        # parity buffers alternate with the staging slot; before overwriting one,
+        # wait only for the host copy that last read it (not for the copy stream)
+        if self._parity is None or self._parity[0][0].numel() < max(hi - lo, 16):
+            self._parity = [[torch.empty(max(hi - lo, 16), dtype=torch.uint8, device=device) for _ in range(spec.m)]
+                            for _ in range(2)]
+            self._parity_free = [None, None]
+        if self._parity_free[slot] is not None:
+            torch.cuda.current_stream(device).wait_event(self._parity_free[slot])
+        parity = self._parity[slot]
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -230,33 +242,31 @@ class KVFaultTolerance:
             data_lo = [self._peers.ptr(r, 2 * slot) for r in range(world)]
             data_hi = [self._peers.ptr(r, 2 * slot + 1) for r in range(world)]
             codec.encode_ptrs(spec, data_lo, data_hi, half, data_bytes,
-                              [t.data_ptr() - lo for t in self._parity], lo, hi)
+                              [t.data_ptr() - lo for t in parity], lo, hi)
         e1.record()
         rec = self._record(chunk_id, -1, None, None, None, spec.m * (hi - lo))
         rec["slice"] = [lo, hi]
         rec["scheme"] = spec.scheme
         if self.cfg.offload and hi > lo:
-            self._offload(rec, [t[:hi - lo] for t in self._parity], e0, e1)
+            self._parity_free[slot] = self._offload(rec, [t[:hi - lo] for t in parity], e0, e1)
         else:
             self._pending.append((rec, None, e0, e1))
         self._drain(block=False)
-        return [t[:hi - lo] for t in self._parity], (lo, hi)
+        return [t[:hi - lo] for t in parity], (lo, hi)
 
     def _offload(self, rec, parity, e0, e1):
+        """Copy parity to the next pinned host ring slot on a side stream; returns
+        the event after which the device parity buffer may be overwritten."""
+        dev = parity[0].device
         if self._copy_stream is None:
-            self._copy_stream = torch.cuda.Stream(parity[0].device)
+            self._copy_stream = torch.cuda.Stream(dev)
         nbytes = sum(t.numel() for t in parity)
-        cur = torch.cuda.current_stream(parity[0].device)
-        self._copy_stream.wait_stream(cur)
-        ring_slot = None
-        if len(self._host) < self.cfg.host_ring:
-            ring_slot = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-            self._host.append(ring_slot)
-        else:
-            ring_slot = self._host[self._calls % len(self._host)]
-            if ring_slot.numel() < nbytes:
-                ring_slot = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-                self._host[self._calls % len(self._host)] = ring_slot
+        if not self._host or self._host[0].numel() < nbytes:
+            # the whole ring is pinned once, up front (pinning is slow)
+            self._host = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(self.cfg.host_ring)]
+        ring_slot = self._host[self._ring_next % len(self._host)]
+        self._ring_next += 1
+        self._copy_stream.wait_stream(torch.cuda.current_stream(dev))
         d0 = torch.cuda.Event(enable_timing=True)
         d1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(self._copy_stream):
@@ -266,10 +276,9 @@ class KVFaultTolerance:
                 ring_slot[off:off + t.numel()].copy_(t, non_blocking=True)
                 off += t.numel()
             d1.record()
-        # the parity buffer is reused next call: order the next encode after this copy
-        cur.wait_stream(self._copy_stream)
         rec["host_parity"] = ring_slot
         self._pending.append((rec, (d0, d1), e0, e1))
+        return d1
 
     def _drain(self, block: bool):
         keep = []
