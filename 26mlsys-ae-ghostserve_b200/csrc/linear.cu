@@ -211,16 +211,20 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
       }
     }
     uint32_t o[4][4];  // [output][word]
+    const bool four = a.nout > 2;  // outputs 2 and 3 need the second half of the transpose
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t u = __byte_perm(acc[w][0], acc[w][1], 0x5140);
       const uint32_t q = __byte_perm(acc[w][2], acc[w][3], 0x5140);
-      const uint32_t u2 = __byte_perm(acc[w][0], acc[w][1], 0x7362);
-      const uint32_t q2 = __byte_perm(acc[w][2], acc[w][3], 0x7362);
       o[0][w] = __byte_perm(u, q, 0x5410);
       o[1][w] = __byte_perm(u, q, 0x7632);
-      o[2][w] = __byte_perm(u2, q2, 0x5410);
-      o[3][w] = __byte_perm(u2, q2, 0x7632);
+      o[2][w] = o[3][w] = 0u;
+      if (four) {
+        const uint32_t u2 = __byte_perm(acc[w][0], acc[w][1], 0x7362);
+        const uint32_t q2 = __byte_perm(acc[w][2], acc[w][3], 0x7362);
+        o[2][w] = __byte_perm(u2, q2, 0x5410);
+        o[3][w] = __byte_perm(u2, q2, 0x7632);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
