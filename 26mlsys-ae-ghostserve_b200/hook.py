@@ -28,6 +28,7 @@ import functools
 import json
 import os
 import time
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -59,7 +60,8 @@ class HookConfig:
     compat_cast_fp16: bool = True       # reference mode: .to(float16) as bench_ghostserve_rdp.py:345-346
     broadcast_chunk_id: bool = True     # reference mode: rank-0 counter + broadcast (:287-301)
     offload: bool = True                # copy parity to pinned host memory
-    host_ring: int = 4                  # pinned parity buffers kept per rank
+    host_keep: int = 256                # chunks whose parity slice stays in pinned host memory
+    host_budget: int = 1 << 30          # bytes of pinned host memory for that store (at least 4 chunks)
     verbose: bool = False
 
 
@@ -75,11 +77,13 @@ class KVFaultTolerance:
         self._staging = None      # fused mode: registered KV staging (2 slots)
         self._peers = None
         self._parity = None
-        self._host = []
+        self._host_block = None   # one pinned block, sliced into per-chunk parity slots
+        self._slot_bytes = 0
+        self._free_slots = []
+        self._store = OrderedDict()  # chunk id -> parity slice record (oldest first)
         self._pending = []        # (record, event, t_enqueue) awaiting D2H completion
         self._copy_stream = None
         self._parity_free = [None, None]
-        self._ring_next = 0
         self._calls = 0
 
     # ------------------------------------------------------------- control --
@@ -191,6 +195,73 @@ class KVFaultTolerance:
         flat = [t for slot in self._staging for t in slot]
         self._peers = p2p.PeerGroup.create(flat, group=self.group)
 
+    def _stage(self, slot, half, parts_k, parts_v):
+        """Copy a shard's K parts then V parts into staging slot `slot`."""
+        for parts, buf in ((parts_k, self._staging[slot][0]), (parts_v, self._staging[slot][1])):
+            if all(t.is_contiguous() for t in parts):
+                torch.cat([t.reshape(-1).view(torch.uint8) for t in parts], out=buf[:half])
+            else:  # strided views: one copy each, straight into the staging buffer
+                off = 0
+                for t in parts:
+                    n = t.numel() * t.element_size()
+                    buf[off:off + n].view(t.dtype).view(t.shape).copy_(t)
+                    off += n
+
+    def _unstage(self, slot, parts_k, parts_v):
+        """Inverse of _stage: scatter staging slot `slot` back into the parts."""
+        for parts, buf in ((parts_k, self._staging[slot][0]), (parts_v, self._staging[slot][1])):
+            off = 0
+            for t in parts:
+                n = t.numel() * t.element_size()
+                t.copy_(buf[off:off + n].view(t.dtype).view(t.shape))
+                off += n
+
+    def recover_parts(self, chunk_id: int, lost, parts_k, parts_v):
+        """Rebuild the KV shard of chunk `chunk_id` on the lost ranks (at most two).
+
+        Collective over the group, replacement ranks included. Surviving ranks
+        pass their chunk's K and V parts (as at encode time) and re-stage them;
+        every rank copies its parity slice of the chunk from the host store back
+        to the device and decodes its stripe slice, reading the survivors'
+        staging with NVLink peer loads and writing the rebuilt stripes straight
+        into the lost ranks' staging buffers; the lost ranks then scatter their
+        staging into `parts_k` / `parts_v`. The host parity store is assumed to
+        outlive a lost GPU (node memory); a parity slice is only recoverable while
+        its chunk is still in the store."""
+        rank, world = self._rank_world()
+        lost = sorted(set(int(r) for r in lost))
+        if not lost:
+            return
+        entry = self._store.get(chunk_id)
+        if entry is None:
+            raise KeyError(f"parity of chunk {chunk_id} is no longer in the host store")
+        spec, half, lo, hi = entry["spec"], entry["half"], entry["lo"], entry["hi"]
+        if len(lost) > spec.m:
+            raise ValueError(f"{len(lost)} lost ranks exceed the code's {spec.m} parity shards")
+        device = parts_k[0].device
+        if sum(t.numel() * t.element_size() for t in parts_k) != half:
+            raise ValueError("parts do not match the encoded chunk size")
+        slot = self._calls % 2
+        self._calls += 1
+        if rank not in lost:
+            self._stage(slot, half, parts_k, parts_v)
+        if hi > lo:
+            if self._parity_free[slot] is not None:
+                torch.cuda.current_stream(device).wait_event(self._parity_free[slot])
+            torch.cuda.current_stream(device).wait_event(entry["copied"])
+            par = self._parity[slot]
+            n = hi - lo
+            for j in range(spec.m):
+                par[j][:n].copy_(entry["host"][j * n:(j + 1) * n], non_blocking=True)
+        self._barrier(device)  # survivors' staging written; every parity slice on its device
+        if hi > lo:
+            shard_lo = [self._peers.ptr(r, 2 * slot) for r in range(world)] + [t.data_ptr() - lo for t in par]
+            shard_hi = [self._peers.ptr(r, 2 * slot + 1) for r in range(world)] + [None] * spec.m
+            codec.decode_ptrs(spec, shard_lo, shard_hi, half, 2 * half, lost, lo, hi)
+        self._barrier(device)  # every slice of the lost shards has landed
+        if rank in lost:
+            self._unstage(slot, parts_k, parts_v)
+
     def encode_chunk(self, local_k: torch.Tensor, local_v: torch.Tensor, chunk_id: int):
         """Fused P2P encode of this rank's slice; returns the device parity slices."""
         return self.encode_parts([local_k], [local_v], chunk_id)
@@ -210,15 +281,7 @@ class KVFaultTolerance:
         self._ensure_staging(half, device)
         slot = self._calls % 2
         self._calls += 1
-        for parts, buf in ((parts_k, self._staging[slot][0]), (parts_v, self._staging[slot][1])):
-            if all(t.is_contiguous() for t in parts):
-                torch.cat([t.reshape(-1).view(torch.uint8) for t in parts], out=buf[:half])
-            else:  # strided views: one copy each, straight into the staging buffer
-                off = 0
-                for t in parts:
-                    n = t.numel() * t.element_size()
-                    buf[off:off + n].view(t.dtype).view(t.shape).copy_(t)
-                    off += n
+        self._stage(slot, half, parts_k, parts_v)
         self._barrier(device)  # every rank's staging write precedes every peer read
         spec = self._spec(world)
         data_bytes = 2 * half
@@ -248,24 +311,36 @@ class KVFaultTolerance:
         rec["slice"] = [lo, hi]
         rec["scheme"] = spec.scheme
         if self.cfg.offload and hi > lo:
-            self._parity_free[slot] = self._offload(rec, [t[:hi - lo] for t in parity], e0, e1)
+            entry = dict(lo=lo, hi=hi, half=half, spec=spec)
+            self._parity_free[slot] = self._offload(rec, [t[:hi - lo] for t in parity], e0, e1, entry)
         else:
             self._pending.append((rec, None, e0, e1))
         self._drain(block=False)
         return [t[:hi - lo] for t in parity], (lo, hi)
 
-    def _offload(self, rec, parity, e0, e1):
-        """Copy parity to the next pinned host ring slot on a side stream; returns
-        the event after which the device parity buffer may be overwritten."""
+    def _host_slot(self, nbytes: int):
+        """A pinned host slot for one chunk's parity slice. The store is one pinned
+        block allocated on first use (pinning is slow) and recycled oldest-first."""
+        if self._host_block is None or self._slot_bytes < nbytes:
+            keep = max(4, min(self.cfg.host_keep, self.cfg.host_budget // max(nbytes, 1)))
+            self._host_block = torch.empty(keep * nbytes, dtype=torch.uint8, pin_memory=True)
+            self._slot_bytes = nbytes
+            self._free_slots = list(range(keep - 1, -1, -1))
+            self._store.clear()
+        if not self._free_slots:
+            _, old = self._store.popitem(last=False)
+            self._free_slots.append(old["slot"])
+        slot = self._free_slots.pop()
+        return slot, self._host_block[slot * self._slot_bytes: slot * self._slot_bytes + nbytes]
+
+    def _offload(self, rec, parity, e0, e1, entry):
+        """Copy this rank's parity slice to its pinned host slot on a side stream;
+        returns the event after which the device parity buffer may be overwritten."""
         dev = parity[0].device
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(dev)
         nbytes = sum(t.numel() for t in parity)
-        if not self._host or self._host[0].numel() < nbytes:
-            # the whole ring is pinned once, up front (pinning is slow)
-            self._host = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(self.cfg.host_ring)]
-        ring_slot = self._host[self._ring_next % len(self._host)]
-        self._ring_next += 1
+        slot, host = self._host_slot(nbytes)
         self._copy_stream.wait_stream(torch.cuda.current_stream(dev))
         d0 = torch.cuda.Event(enable_timing=True)
         d1 = torch.cuda.Event(enable_timing=True)
@@ -273,10 +348,11 @@ class KVFaultTolerance:
             d0.record()
             off = 0
             for t in parity:
-                ring_slot[off:off + t.numel()].copy_(t, non_blocking=True)
+                host[off:off + t.numel()].copy_(t, non_blocking=True)
                 off += t.numel()
             d1.record()
-        rec["host_parity"] = ring_slot
+        entry.update(slot=slot, host=host, copied=d1)
+        self._store[rec["chunk_id"]] = entry
         self._pending.append((rec, (d0, d1), e0, e1))
         return d1
 
@@ -295,7 +371,6 @@ class KVFaultTolerance:
                     continue
                 d2h[1].synchronize()
                 rec["timings"]["gpu_to_cpu_ms"] = float(d2h[0].elapsed_time(d2h[1]))
-            rec.pop("host_parity", None)
             self._emit(rec)
         self._pending = keep
 

@@ -159,3 +159,50 @@ def hook_fused(rank, world, port, backend, unit, out):
     recs = [r["chunk_id"] for r in ft.records]
     out.put((rank, ok, recs))
     dist.destroy_process_group()
+
+
+def hook_recover(rank, world, port, backend, scheme, lost_sets, out):
+    """Encode several prefill chunks of a layer-major KV cache through the hook,
+    then lose ranks (their chunk KV zeroed, as on a replacement GPU) and rebuild
+    it with KVFaultTolerance.recover_parts; every rebuilt byte must match."""
+    _init(rank, world, port, backend)
+    dev = rank if backend == "nccl" else 0
+    torch.cuda.set_device(dev)
+    hook = _pkg("hook")
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme=scheme, unit=512, host_keep=4,
+                                               metrics_file=None))
+    layers, hk, tmax, d = 3, 2, 256, 64
+    gen = torch.Generator(device="cuda").manual_seed(11 + rank)
+    kc = torch.randn(layers, hk, tmax, d, device="cuda", generator=gen).to(torch.bfloat16)
+    vc = torch.randn(layers, hk, tmax, d, device="cuda", generator=gen).to(torch.bfloat16)
+
+    def parts(pos0, t):
+        return ([kc[li, :, pos0:pos0 + t] for li in range(layers)],
+                [vc[li, :, pos0:pos0 + t] for li in range(layers)])
+
+    chunks = [(c + 1, 40 * c, 40) for c in range(6)]
+    for cid, pos0, t in chunks:
+        ft.encode_parts(*parts(pos0, t), cid)
+    ft.flush()
+    ok = True
+    for lost in lost_sets:
+        for cid, pos0, t in chunks[2:]:
+            pk, pv = parts(pos0, t)
+            want = [x.clone() for x in pk + pv]
+            if rank in lost:
+                for x in pk + pv:
+                    x.fill_(0)
+            ft.recover_parts(cid, lost, pk, pv)
+            torch.cuda.synchronize()
+            ok = ok and all(torch.equal(a, b) for a, b in zip(pk + pv, want))
+    evicted = True
+    try:
+        ft.recover_parts(1, lost_sets[0], *parts(0, 40))
+        evicted = False
+    except KeyError:
+        pass
+    ft.close()
+    oks = [None] * world
+    dist.all_gather_object(oks, ok)
+    out.put((rank, all(oks), evicted))
+    dist.destroy_process_group()

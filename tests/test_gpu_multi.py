@@ -19,3 +19,12 @@ def test_hook_fused_mode_two_gpus(unit):
     assert res[0][1] is True
     for _rank, _ok, recs in res:
         assert recs == [1, 2, 3]
+
+
+@pytest.mark.parametrize("scheme,lost_sets", [("rdp", [[1], [0], [0, 1]]), ("rs8", [[0], [1], [0, 1]]),
+                                              ("xor", [[1], [0]])])
+def test_hook_recover_lost_ranks_two_gpus(scheme, lost_sets):
+    res = run_ranks(mp_workers.hook_recover, 2, "nccl", scheme, lost_sets, timeout=300)
+    for _rank, ok, evicted in res:
+        assert ok is True
+        assert evicted is True
