@@ -340,6 +340,9 @@ class KVFaultTolerance:
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(dev)
         nbytes = sum(t.numel() for t in parity)
+        old = self._store.pop(rec["chunk_id"], None)
+        if old is not None:  # a chunk id encoded again replaces its earlier parity
+            self._free_slots.append(old["slot"])
         slot, host = self._host_slot(nbytes)
         self._copy_stream.wait_stream(torch.cuda.current_stream(dev))
         d0 = torch.cuda.Event(enable_timing=True)

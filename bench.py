@@ -436,6 +436,7 @@ def run_prefill_bench(args):
     chunk = args.prefill_chunk
     variants = [v for v in args.parity.split(",") if v]
     rates, times = {}, {}
+    recovery = None
     for var in variants:
         ft = None
         if var != "none":
@@ -455,6 +456,8 @@ def run_prefill_bench(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times[var] = float(t.item())
         rates[var] = tokens / (times[var] * 1e-3)
+        if var == "fused":
+            recovery = measure_recovery(torch, dist, model, ft, args, device)
         if ft is not None:
             ft.close()
     base = rates.get("none")
@@ -472,9 +475,60 @@ def run_prefill_bench(args):
             "overhead_pct": {k: round(100.0 * (base / v - 1.0), 2) for k, v in rates.items()
                              if base and k != "none"},
         }
+        if recovery is not None:
+            line["recover"] = recovery
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def measure_recovery(torch, dist, model, ft, args, device):
+    """Rebuild the last sequence's chunk KV of lost rank(s) from the host parity
+    store (KVFaultTolerance.recover_parts): one lost rank (rank 1, or 0 at TP=1)
+    and, for TP >= 2, ranks 0 and 1 together. The lost ranks' chunk KV is zeroed
+    first and compared with a saved copy afterwards. Time per chunk = max over
+    ranks of CUDA-event time over the chunks still held."""
+    chunk, n = args.prefill_chunk, args.prefill_len
+    rank, world = ft._rank_world()
+    per_seq = (n + chunk - 1) // chunk
+    last = args.prefill_seqs * per_seq  # chunk id of the last chunk
+    # the last sequence's chunks whose parity is still in the host store
+    held = [(cid, pos0) for cid, pos0 in zip(range(last - per_seq + 1, last + 1), range(0, n, chunk))
+            if cid in ft._store]
+    out = {"chunks_held": len(held), "chunks_in_sequence": per_seq}
+    for lost in ([1], [0, 1]) if world >= 2 else ([0],):
+        saved = []
+        for _cid, pos0 in held:
+            pk, pv = model.chunk_kv_parts(pos0, min(chunk, n - pos0))
+            saved.append([x.clone() for x in pk + pv] if rank in lost else None)
+            if rank in lost:
+                for x in pk + pv:
+                    x.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rebuilt = 0
+        for cid, pos0 in held:
+            pk, pv = model.chunk_kv_parts(pos0, min(chunk, n - pos0))
+            ft.recover_parts(cid, lost, pk, pv)
+            rebuilt += len(lost) * 2 * sum(x.numel() * x.element_size() for x in pk)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ok = True
+        if rank in lost:
+            for i, (_cid, pos0) in enumerate(held):
+                pk, pv = model.chunk_kv_parts(pos0, min(chunk, n - pos0))
+                ok = ok and all(torch.equal(a, b) for a, b in zip(pk + pv, saved[i]))
+        okt = torch.tensor([0 if ok else 1], device=device, dtype=torch.int32)
+        dist.all_reduce(okt, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        out["lost_" + "_".join(map(str, lost))] = {
+            "ms_per_chunk": round(ms / max(len(held), 1), 3),
+            "rebuilt_GB_s": round(rebuilt / (ms * 1e-3) / 1e9, 2), "verified": int(okt.item()) == 0}
+    return out
 
 
 def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):

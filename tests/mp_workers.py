@@ -183,6 +183,7 @@ def hook_recover(rank, world, port, backend, scheme, lost_sets, out):
     chunks = [(c + 1, 40 * c, 40) for c in range(6)]
     for cid, pos0, t in chunks:
         ft.encode_parts(*parts(pos0, t), cid)
+    ft.encode_parts(*parts(200, 40), 6)  # an id encoded again keeps one store slot
     ft.flush()
     ok = True
     for lost in lost_sets:
