@@ -380,6 +380,7 @@ int gsec_decode(const gsec_code* code, void* const* shard_lo, void* const* shard
       a.out_lo[e] = lo(erased[e]);
       a.out_hi[e] = hi(erased[e]);
     }
+    rdp_build_program(a);
     return rdp_decode(a, s);
   }
 

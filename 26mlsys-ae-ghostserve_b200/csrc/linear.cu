@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       pipe::bar_init(full + s, 1);
-      pipe::bar_init(empty + s, kLLanes);
+      pipe::bar_init(empty + s, kLLanes / 32);
     }
     pipe::bar_init_fence();
   }
@@ -94,32 +94,28 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
   const int64_t vend = a.begin + (((a.end - a.begin) >> 4) << 4);  // end of the whole-vector part
   const int64_t items = (vend - a.begin + kLSeg - 1) / kLSeg;
 
-  if (threadIdx.x >= kLLanes) {  // producer warp
-    if (threadIdx.x != kLLanes) return;
+  if (threadIdx.x >= kLLanes) {  // producer warp: lane i copies input i of each stage
+    const int pl = threadIdx.x - kLLanes;
+    const bool mine = pl < nin;
+    const char* my_lo = mine ? a.in_lo[pl] : nullptr;
+    const char* my_hi = mine ? a.in_hi[pl] : nullptr;
     pipe::Ring r;
     int64_t filled = 0;
     for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
-      if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
-        atomicOr(&g_linear_status, 1u);
-        pipe::producer_drain(full, nst, r, filled);
+      if (!pipe::warp_acquire(empty, r, filled, nst, pl)) {
+        if (pl == 0) {
+          atomicOr(&g_linear_status, 1u);
+          pipe::producer_drain(full, nst, r, filled);
+        }
         return;
       }
       const int64_t off = a.begin + it * kLSeg;
       const int64_t bytes = vend - off < kLSeg ? vend - off : kLSeg;
-      pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * nin));
-      unsigned char* dst = smem + (size_t)r.stage * stage_bytes;
-      for (int i = 0; i < nin; ++i) {
-        unsigned char* d = dst + i * kLSeg;
-        if (off + bytes <= a.split) {
-          pipe::bulk_load(d, a.in_lo[i] + off, (uint32_t)bytes, full + r.stage);
-        } else if (off >= a.split) {
-          pipe::bulk_load(d, a.in_hi[i] + (off - a.split), (uint32_t)bytes, full + r.stage);
-        } else {
-          const uint32_t b0 = (uint32_t)(a.split - off);
-          pipe::bulk_load(d, a.in_lo[i] + off, b0, full + r.stage);
-          pipe::bulk_load(d + b0, a.in_hi[i], (uint32_t)bytes - b0, full + r.stage);
-        }
-      }
+      if (pl == 0) pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * nin));
+      __syncwarp();
+      if (mine)
+        pipe::bulk_load_split(smem + (size_t)r.stage * stage_bytes + pl * kLSeg, my_lo, my_hi, a.split, off,
+                              (uint32_t)bytes, full + r.stage);
       r.next(nst);
       ++filled;
     }
@@ -138,7 +134,7 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
     uint4 acc = vzero();
     if (off < vend)
       for (int i = 0; i < nin; ++i) acc = vxor(acc, st[i * kLLanes]);
-    pipe::bar_arrive(empty + r.stage);
+    pipe::warp_release(empty + r.stage);
     r.next(nst);
     if (off < vend)
       for (int o = 0; o < a.nout; ++o)

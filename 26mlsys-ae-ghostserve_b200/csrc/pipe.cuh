@@ -65,6 +65,27 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// bulk_load of bytes [off, off + bytes) of the two-segment string lo[0..split) ++ hi[0..).
+__device__ __forceinline__ void bulk_load_split(void* dst, const char* lo, const char* hi, int64_t split,
+                                                int64_t off, uint32_t bytes, uint64_t* bar) {
+  if (off + bytes <= split) {
+    bulk_load(dst, lo + off, bytes, bar);
+  } else if (off >= split) {
+    bulk_load(dst, hi + (off - split), bytes, bar);
+  } else {  // the boundary falls inside this copy
+    const uint32_t b0 = (uint32_t)(split - off);
+    bulk_load(dst, lo + off, b0, bar);
+    bulk_load(static_cast<char*>(dst) + b0, hi, bytes - b0, bar);
+  }
+}
+
+// Consumer side: every lane of the warp has finished reading the stage; one
+// arrival per warp (the empty barrier counts warps).
+__device__ __forceinline__ void warp_release(uint64_t* b) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) bar_arrive(b);
+}
+
 // Iteration state of one side of a ring of `nst` stages.
 struct Ring {
   int stage = 0;
@@ -76,6 +97,16 @@ struct Ring {
     }
   }
 };
+
+// Producer warp: lane 0 waits (bounded) until the consumers have released
+// stage r.stage (nothing to wait for while the ring is first being filled);
+// the outcome is broadcast to the warp. `lane` = lane index in the warp.
+__device__ __forceinline__ bool warp_acquire(uint64_t* empty, const Ring& r, int64_t filled, int nst, int lane) {
+  if (filled < nst) return true;
+  bool ok = true;
+  if (lane == 0) ok = bar_wait(empty + r.stage, r.phase ^ 1u);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
 
 // Producer side: after a failed acquire, wait for the last stages it filled
 // (their copies) before returning. `filled` = number of stages filled so far.

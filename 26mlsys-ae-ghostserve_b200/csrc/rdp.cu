@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const Rd
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       pipe::bar_init(full + s, 1);
-      pipe::bar_init(empty + s, kSegLanes);
+      pipe::bar_init(empty + s, kSegLanes / 32);
     }
     pipe::bar_init_fence();
   }
@@ -114,38 +114,32 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const Rd
   const int64_t items = (a.s_end - a.s_begin) * spu;
   const int64_t sb = (int64_t)(P - 1) * a.unit;
 
-  if (threadIdx.x >= kSegLanes) {  // producer warp
-    if (threadIdx.x != kSegLanes) return;
+  if (threadIdx.x >= kSegLanes) {  // producer warp: lane c copies column c of each stage
+    const int pl = threadIdx.x - kSegLanes;
+    const bool mine = pl < k;
+    const char* my_lo = mine ? a.d_lo[pl] : nullptr;
+    const char* my_hi = mine ? a.d_hi[pl] : nullptr;
     pipe::Ring r;
     int64_t filled = 0;
     for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
       const int64_t stripe = a.s_begin + it / spu;
       const int64_t seg0 = (it % spu) * kSeg;
       for (int row = 0; row < P - 1; ++row) {
-        if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
-          atomicOr(&g_rdp_status, 1u);
-          pipe::producer_drain(full, nst, r, filled);
+        if (!pipe::warp_acquire(empty, r, filled, nst, pl)) {
+          if (pl == 0) {
+            atomicOr(&g_rdp_status, 1u);
+            pipe::producer_drain(full, nst, r, filled);
+          }
           return;
         }
         const int64_t off = stripe * sb + (int64_t)row * a.unit + seg0;
         int64_t bytes = a.data_bytes - off;
         bytes = bytes < 0 ? 0 : (bytes > kSeg ? kSeg : bytes);
-        pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * k));
-        unsigned char* dst = smem + (size_t)r.stage * stage_bytes;
-        if (bytes > 0) {
-          for (int c = 0; c < k; ++c) {
-            unsigned char* d = dst + c * kSeg;
-            if (off + bytes <= a.split) {
-              pipe::bulk_load(d, a.d_lo[c] + off, (uint32_t)bytes, full + r.stage);
-            } else if (off >= a.split) {
-              pipe::bulk_load(d, a.d_hi[c] + (off - a.split), (uint32_t)bytes, full + r.stage);
-            } else {  // the K|V boundary falls inside this segment
-              const uint32_t b0 = (uint32_t)(a.split - off);
-              pipe::bulk_load(d, a.d_lo[c] + off, b0, full + r.stage);
-              pipe::bulk_load(d + b0, a.d_hi[c], (uint32_t)bytes - b0, full + r.stage);
-            }
-          }
-        }
+        if (pl == 0) pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * k));
+        __syncwarp();
+        if (mine && bytes > 0)
+          pipe::bulk_load_split(smem + (size_t)r.stage * stage_bytes + pl * kSeg, my_lo, my_hi, a.split, off,
+                                (uint32_t)bytes, full + r.stage);
         r.next(nst);
         ++filled;
       }
@@ -179,7 +173,7 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const Rd
           if ((row + c) % P != P - 1) q[(row + c) % P] = vxor(q[(row + c) % P], x);
         }
       }
-      pipe::bar_arrive(empty + r.stage);
+      pipe::warp_release(empty + r.stage);
       r.next(nst);
       st16(a.parity[0] + off, prow);
       if ((row + P - 1) % P != P - 1) q[(row + P - 1) % P] = vxor(q[(row + P - 1) % P], prow);
@@ -242,18 +236,32 @@ __global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) 
 // rdp_decode_kernel's syndrome decode with the surviving cells staged in shared
 // memory: one ring stage = row r of every surviving column of the item
 // (stripe, 1 KiB segment), packed in column order.
+// Warps of one CTA: 0-1 accumulate syndromes (one 16-byte lane column of the
+// 1 KiB segment each), 2-3 write the erased cells, 4 issues the bulk copies.
+constexpr int kDecThreads = 2 * kSegLanes + 32;
+
 template <int P>
-__global__ void __launch_bounds__(kSegLanes + 32) rdp_decode_tma_kernel(const RdpDecodeArgs a, int nst) {
+__global__ void __launch_bounds__(kDecThreads) rdp_decode_tma_kernel(const RdpDecodeArgs a, int nst) {
   constexpr int NS = 2 * (P - 1);
   extern __shared__ __align__(128) unsigned char smem[];
   const int nalive = __popc(a.alive);
   const int stage_bytes = nalive * kSeg;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes);
+  // After the ring: two syndrome buffers [2][NS][kSegLanes] handed from the
+  // accumulating warps to the writing warps, so an item's erased cells are
+  // written while the next item's rows are being accumulated.
+  uint4* synsm = reinterpret_cast<uint4*>(smem + (size_t)nst * stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes + (size_t)2 * NS * kSeg);
   uint64_t* empty = full + nst;
+  uint64_t* sfull = empty + nst;  // [2]: syndromes of an item are in the buffer
+  uint64_t* sempty = sfull + 2;   // [2]: the writers are done with the buffer
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       pipe::bar_init(full + s, 1);
-      pipe::bar_init(empty + s, kSegLanes);
+      pipe::bar_init(empty + s, kSegLanes / 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      pipe::bar_init(sfull + b, kSegLanes / 32);
+      pipe::bar_init(sempty + b, kSegLanes / 32);
     }
     pipe::bar_init_fence();
   }
@@ -262,46 +270,66 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_decode_tma_kernel(const Rd
   const int64_t items = (a.s_end - a.s_begin) * spu;
   const int64_t sb = (int64_t)(P - 1) * a.unit;
 
-  if (threadIdx.x >= kSegLanes) {  // producer warp
-    if (threadIdx.x != kSegLanes) return;
+  if (threadIdx.x >= 2 * kSegLanes) {  // producer warp: lane j copies the j-th alive column
+    const int pl = threadIdx.x - 2 * kSegLanes;
+    int col = -1;
+    for (uint32_t live = a.alive, j = 0; live; live &= live - 1u, ++j)
+      if ((int)j == pl) col = __ffs(live) - 1;
+    const char* my_lo = col >= 0 ? a.lo[col] : nullptr;
+    const char* my_hi = col >= 0 ? a.hi[col] : nullptr;
+    const bool my_data = col >= 0 && col < P - 1;
+    const uint32_t ndata = __popc(a.alive & ((1u << (P - 1)) - 1u));  // alive data columns
+    const uint32_t npar = (uint32_t)nalive - ndata;                   // alive P / Q
     pipe::Ring r;
     int64_t filled = 0;
     for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
       const int64_t stripe = a.s_begin + it / spu;
       const int64_t seg0 = (it % spu) * kSeg;
       for (int row = 0; row < P - 1; ++row) {
-        if (filled >= nst && !pipe::bar_wait(empty + r.stage, r.phase ^ 1u)) {
-          atomicOr(&g_rdp_status, 4u);
-          pipe::producer_drain(full, nst, r, filled);
+        if (!pipe::warp_acquire(empty, r, filled, nst, pl)) {
+          if (pl == 0) {
+            atomicOr(&g_rdp_status, 4u);
+            pipe::producer_drain(full, nst, r, filled);
+          }
           return;
         }
         const int64_t off = stripe * sb + (int64_t)row * a.unit + seg0;
         int64_t dbytes = a.data_bytes - off;
         dbytes = dbytes < 0 ? 0 : (dbytes > kSeg ? kSeg : dbytes);
-        uint32_t tx = 0;
-        for (int c = 0; c <= P; ++c)
-          if ((a.alive >> c) & 1u) tx += (uint32_t)(c < P - 1 ? dbytes : kSeg);
-        pipe::bar_expect_tx(full + r.stage, tx);
-        unsigned char* d = smem + (size_t)r.stage * stage_bytes;
-        for (int c = 0; c <= P; ++c) {
-          if (!((a.alive >> c) & 1u)) continue;
-          const int64_t bytes = c < P - 1 ? dbytes : kSeg;
-          if (bytes > 0) {
-            if (off + bytes <= a.split) {
-              pipe::bulk_load(d, a.lo[c] + off, (uint32_t)bytes, full + r.stage);
-            } else if (off >= a.split) {
-              pipe::bulk_load(d, a.hi[c] + (off - a.split), (uint32_t)bytes, full + r.stage);
-            } else {
-              const uint32_t b0 = (uint32_t)(a.split - off);
-              pipe::bulk_load(d, a.lo[c] + off, b0, full + r.stage);
-              pipe::bulk_load(d + b0, a.hi[c], (uint32_t)bytes - b0, full + r.stage);
-            }
-          }
-          d += kSeg;
-        }
+        if (pl == 0) pipe::bar_expect_tx(full + r.stage, ndata * (uint32_t)dbytes + npar * (uint32_t)kSeg);
+        __syncwarp();
+        const int64_t bytes = my_data ? dbytes : kSeg;
+        if (col >= 0 && bytes > 0)
+          pipe::bulk_load_split(smem + (size_t)r.stage * stage_bytes + pl * kSeg, my_lo, my_hi, a.split, off,
+                                (uint32_t)bytes, full + r.stage);
         r.next(nst);
         ++filled;
       }
+    }
+    return;
+  }
+
+  if (threadIdx.x >= kSegLanes) {  // writer warps: the erased cells as a chain program
+    const int lane = threadIdx.x - kSegLanes;
+    pipe::Ring sb_r;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+      if (!pipe::bar_wait(sfull + sb_r.stage, sb_r.phase)) {
+        atomicOr(&g_rdp_status, 16u);
+        return;
+      }
+      const uint4* syn = synsm + (size_t)sb_r.stage * NS * kSegLanes + lane;
+      const int64_t stripe = a.s_begin + it / spu;
+      const int64_t base = stripe * sb + (it % spu) * kSeg + lane * 16;
+      uint4 o = vzero();
+      for (int t = 0; t < a.nprog; ++t) {
+        if (!a.prog_chain[t]) o = vzero();
+        for (uint32_t dm = a.prog_diff[t]; dm; dm &= dm - 1u) o = vxor(o, syn[(__ffs(dm) - 1) * kSegLanes]);
+        const int e = a.prog_out[t] >> 4;
+        const int64_t off = base + (int64_t)(a.prog_out[t] & 15) * a.unit;
+        if (a.out_col[e] >= P - 1 || off < a.data_bytes) st16(seg(a.out_lo[e], a.out_hi[e], a.split, off), o);
+      }
+      pipe::warp_release(sempty + sb_r.stage);
+      sb_r.next(2);
     }
     return;
   }
@@ -311,6 +339,8 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_decode_tma_kernel(const Rd
 #pragma unroll
   for (int c = 0; c <= P; ++c) pos[c] = __popc(a.alive & ((1u << c) - 1u)) * kSegLanes;
   pipe::Ring r;
+  pipe::Ring sb_r;
+  int64_t handed = 0;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
     const int64_t stripe = a.s_begin + it / spu;
     const int64_t base = stripe * sb + (it % spu) * kSeg + lane * 16;
@@ -338,22 +368,20 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_decode_tma_kernel(const Rd
           syn[(P - 1) + row] = vxor(syn[(P - 1) + row], v);
         }
       }
-      pipe::bar_arrive(empty + r.stage);
+      pipe::warp_release(empty + r.stage);
       r.next(nst);
     }
-    for (int e = 0; e < a.nout; ++e) {
-      const bool out_data = a.out_col[e] < P - 1;
-#pragma unroll
-      for (int row = 0; row < P - 1; ++row) {
-        const int64_t off = base + (int64_t)row * a.unit;
-        const uint32_t m = a.mask[e][row];
-        uint4 o = vzero();
-#pragma unroll
-        for (int j = 0; j < NS; ++j)
-          if ((m >> j) & 1u) o = vxor(o, syn[j]);
-        if (!out_data || off < a.data_bytes) st16(seg(a.out_lo[e], a.out_hi[e], a.split, off), o);
-      }
+    // hand the syndromes to the writers (wait until they are done with the buffer)
+    if (handed >= 2 && !pipe::bar_wait(sempty + sb_r.stage, sb_r.phase ^ 1u)) {
+      atomicOr(&g_rdp_status, 32u);
+      return;
     }
+    uint4* dst = synsm + (size_t)sb_r.stage * NS * kSegLanes + lane;
+#pragma unroll
+    for (int j = 0; j < NS; ++j) dst[j * kSegLanes] = syn[j];
+    pipe::warp_release(sfull + sb_r.stage);
+    sb_r.next(2);
+    ++handed;
   }
 }
 
@@ -368,8 +396,18 @@ int grid_for(K kernel, int threads, int64_t items) {
   return (int)(grid < 1 ? 1 : grid);
 }
 
-constexpr int kStages = 3;
-constexpr int kCtasPerSm = 5;
+#ifndef GSEC_RDP_STAGES
+#define GSEC_RDP_STAGES 3
+#endif
+#ifndef GSEC_RDP_CTAS
+#define GSEC_RDP_CTAS 5
+#endif
+#ifndef GSEC_RDP_DEC_STAGES
+#define GSEC_RDP_DEC_STAGES 4
+#endif
+constexpr int kStages = GSEC_RDP_STAGES;   // ring stages per CTA
+constexpr int kDecStages = GSEC_RDP_DEC_STAGES;  // the decode's (its items end in a burst of stores)
+constexpr int kCtasPerSm = GSEC_RDP_CTAS;  // resident CTAs per SM (at most)
 
 template <int P>
 int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
@@ -397,14 +435,15 @@ int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
   if (a.unit % kSeg == 0) {
     LaunchCache& cache = launch_cache();
     auto k = rdp_decode_tma_kernel<P>;
-    const size_t smem = (size_t)kStages * __builtin_popcount(a.alive) * kSeg + 2 * kStages * sizeof(uint64_t);
-    int per_sm = cache.blocks_per_sm(k, kSegLanes + 32, smem);
+    const size_t smem = (size_t)kDecStages * __builtin_popcount(a.alive) * kSeg + (size_t)2 * 2 * (P - 1) * kSeg +
+                        (2 * kDecStages + 4) * sizeof(uint64_t);
+    int per_sm = cache.blocks_per_sm(k, kDecThreads, smem);
     if (per_sm < 0) return check_launch("rdp_decode_tma launch shape");
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
     int64_t grid = (int64_t)sm_count() * per_sm;
     if (grid > items) grid = items;
-    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, kStages);
+    k<<<(int)grid, kDecThreads, smem, s>>>(a, kDecStages);
     return check_launch("rdp_decode_tma_kernel");
   }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
@@ -505,6 +544,43 @@ int rdp_solve_masks(int p, const int* cols, int ncols, uint32_t mask[2][16]) {
   for (int e = 0; e < ncols; ++e)
     for (int r = 0; r < rows; ++r) mask[e][r] = rhs[pivot_of[e * rows + r]];
   return GSEC_OK;
+}
+
+// Greedy chain over the erased cells: each step takes the unsolved cell whose
+// syndrome set differs least from the previous step's (reusing that cell), or
+// starts afresh when that is cheaper. For two erased data columns this finds
+// RDP's alternating row/diagonal recovery chains: one syndrome per cell after
+// the first.
+void rdp_build_program(RdpDecodeArgs& a) {
+  const int rows = a.p - 1;
+  const int n = a.nout * rows;
+  bool done[32] = {};
+  uint32_t prev = 0;
+  bool have_prev = false;
+  for (int t = 0; t < n; ++t) {
+    int best = -1, best_cost = 1 << 30;
+    bool best_chain = false;
+    for (int u = 0; u < n; ++u) {
+      if (done[u]) continue;
+      const uint32_t m = a.mask[u / rows][u % rows];
+      const int fresh = __builtin_popcount(m);
+      const int chained = have_prev ? __builtin_popcount(m ^ prev) : 1 << 30;
+      const int cost = chained <= fresh ? chained : fresh;
+      if (cost < best_cost) {
+        best = u;
+        best_cost = cost;
+        best_chain = chained <= fresh;
+      }
+    }
+    const uint32_t m = a.mask[best / rows][best % rows];
+    done[best] = true;
+    a.prog_out[t] = (uint8_t)(((best / rows) << 4) | (best % rows));
+    a.prog_chain[t] = best_chain ? 1 : 0;
+    a.prog_diff[t] = best_chain ? (m ^ prev) : m;
+    prev = m;
+    have_prev = true;
+  }
+  a.nprog = n;
 }
 
 }  // namespace gsec

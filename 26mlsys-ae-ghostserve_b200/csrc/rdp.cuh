@@ -25,6 +25,13 @@ struct RdpDecodeArgs {
   char* out_lo[2];
   char* out_hi[2];
   uint32_t mask[2][16];  // per erased column and row: syndromes to XOR
+  // The same solution as a straight-line program over the erased cells: step t
+  // rebuilds cell (prog_out[t] >> 4 = erased column index, & 15 = row) as
+  // (prog_chain[t] ? cell of step t-1 : 0) ^ XOR of the syndromes in prog_diff[t].
+  uint32_t prog_diff[32];
+  uint8_t prog_out[32];
+  uint8_t prog_chain[32];
+  int nprog;
   int out_col[2];
   int nout;
   uint32_t alive;        // bit c set: column c is read
@@ -41,5 +48,8 @@ unsigned rdp_device_status(bool clear);
 int rdp_encode(const RdpEncodeArgs& a, cudaStream_t s);
 int rdp_decode(const RdpDecodeArgs& a, cudaStream_t s);
 int rdp_solve_masks(int p, const int* cols, int ncols, uint32_t mask[2][16]);
+// Order the erased cells of a solved pattern into a chain program (fills
+// prog_* and nprog of `a` from a.mask, a.nout and a.p).
+void rdp_build_program(RdpDecodeArgs& a);
 
 }  // namespace gsec

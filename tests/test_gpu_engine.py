@@ -74,9 +74,9 @@ def test_rdp_encode_matches_oracle(rng, p, k, unit):
 
 
 @pytest.mark.parametrize("p,k", RDP_CASES)
-def test_rdp_decodes_every_pattern(rng, p, k):
+@pytest.mark.parametrize("unit", [64, 1024])  # per-thread kernel, TMA-staged kernel
+def test_rdp_decodes_every_pattern(rng, p, k, unit):
     g = pkg()
-    unit = 64
     spec = g.CodeSpec.rdp(k, p, unit)
     data_bytes = 3 * (p - 1) * unit + 5 * 16
     data = [rand_bytes(rng, data_bytes) for _ in range(k)]
