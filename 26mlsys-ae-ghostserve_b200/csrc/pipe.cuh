@@ -101,7 +101,7 @@ struct Ring {
 // Producer warp: lane 0 waits (bounded) until the consumers have released
 // stage r.stage (nothing to wait for while the ring is first being filled);
 // the outcome is broadcast to the warp. `lane` = lane index in the warp.
-__device__ __forceinline__ bool warp_acquire(uint64_t* empty, const Ring& r, int64_t filled, int nst, int lane) {
+__device__ __forceinline__ bool warp_acquire(uint64_t* empty, Ring r, int64_t filled, int nst, int lane) {
   if (filled < nst) return true;
   bool ok = true;
   if (lane == 0) ok = bar_wait(empty + r.stage, r.phase ^ 1u);
