@@ -139,6 +139,54 @@ def decode_ptrs(spec: CodeSpec, shard_lo: Sequence[int], shard_hi: Optional[Sequ
               _lib.C.c_void_p(stream if stream is not None else stream_handle()))
 
 
+def _pool_geometry(pool: torch.Tensor, plane: int):
+    """(row bytes, slot pitch, plane byte offset) of a KV pool [slots, planes, ...]."""
+    if not isinstance(pool, torch.Tensor) or not pool.is_cuda or pool.dim() < 2:
+        raise ValueError("pool must be a CUDA tensor [slots, planes, ...]")
+    if not 0 <= plane < pool.shape[1]:
+        raise ValueError(f"plane {plane} out of range for a pool of {pool.shape[1]} planes")
+    if not pool[0, 0].is_contiguous():
+        raise ValueError("a pool row (pool[slot, plane]) must be contiguous")
+    es = pool.element_size()
+    return pool[0, 0].numel() * es, pool.stride(0) * es, plane * pool.stride(1) * es
+
+
+def _slot_list(slots: torch.Tensor, device) -> torch.Tensor:
+    if not isinstance(slots, torch.Tensor) or slots.device != device:
+        raise ValueError("slots must be a tensor on the pool's device")
+    if slots.dtype not in (torch.int32, torch.int64) or not slots.is_contiguous():
+        raise ValueError("slots must be a contiguous int32 or int64 tensor")
+    return slots
+
+
+def slots_gather(pool: torch.Tensor, slots: torch.Tensor, out: torch.Tensor, plane: int = 0,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """out[i] = pool[slots[i], plane] for every list position (zero rows for
+    negative slots), as bytes: out holds len(slots) rows back to back."""
+    row, pitch, off = _pool_geometry(pool, plane)
+    slots = _slot_list(slots, pool.device)
+    n = slots.numel()
+    _check_tensor(out, "out")
+    if _nbytes(out) < n * row:
+        raise ValueError(f"out holds {_nbytes(out)} bytes, needs {n * row}")
+    _lib.call("gsec_slots_gather", pool.data_ptr() + off, pitch, 0, 1, row, slots.data_ptr(),
+              slots.element_size(), n, pool.shape[0], out.data_ptr(), stream_handle(stream))
+    return out
+
+
+def slots_scatter(pool: torch.Tensor, slots: torch.Tensor, src: torch.Tensor, plane: int = 0,
+                  stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Inverse of slots_gather: pool[slots[i], plane] = src row i (negative slots skipped)."""
+    row, pitch, off = _pool_geometry(pool, plane)
+    slots = _slot_list(slots, pool.device)
+    n = slots.numel()
+    _check_tensor(src, "src")
+    if _nbytes(src) < n * row:
+        raise ValueError(f"src holds {_nbytes(src)} bytes, needs {n * row}")
+    _lib.call("gsec_slots_scatter", pool.data_ptr() + off, pitch, 0, 1, row, slots.data_ptr(),
+              slots.element_size(), n, pool.shape[0], src.data_ptr(), stream_handle(stream))
+
+
 class PreparedEncode:
     """One gsec_encode call with its arguments marshalled once.
 

@@ -241,7 +241,10 @@ int gsec_device_status(uint32_t* status, int32_t clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("device synchronize");
   const unsigned v1 = rdp_device_status(clear != 0);
   const unsigned v2 = linear_device_status(clear != 0);
-  const unsigned v = (v1 == 0xffffffffu || v2 == 0xffffffffu) ? 0xffffffffu : (v1 | (v2 << 8));
+  const unsigned v3 = layout_device_status(clear != 0);
+  const unsigned v = (v1 == 0xffffffffu || v2 == 0xffffffffu || v3 == 0xffffffffu)
+                         ? 0xffffffffu
+                         : (v1 | (v2 << 8) | (v3 << 16));
   if (v == 0xffffffffu) {
     set_error("cannot read the device status word");
     return GSEC_ECUDA;
@@ -444,6 +447,26 @@ int gsec_rows_pack(const void* src0, int64_t len0, const void* src1, int64_t len
 int gsec_rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int32_t nrows, void* dst0, int64_t len0,
                      void* dst1, int64_t len1, gsec_stream_t stream) {
   return rows_unpack(rows, pitch, row_bytes, nrows, dst0, len0, dst1, len1, as_stream(stream));
+}
+
+int gsec_slots_gather(const void* pool, int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes,
+                      const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows, void* dst,
+                      gsec_stream_t stream) {
+  GSEC_REQUIRE(pool != nullptr && dst != nullptr && (n == 0 || slots != nullptr), "null pointer");
+  GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
+  GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
+  return slots_move(true, const_cast<void*>(pool), pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                    dst, as_stream(stream));
+}
+
+int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes,
+                       const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows, const void* src,
+                       gsec_stream_t stream) {
+  GSEC_REQUIRE(pool != nullptr && src != nullptr && (n == 0 || slots != nullptr), "null pointer");
+  GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
+  GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
+  return slots_move(false, pool, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                    const_cast<void*>(src), as_stream(stream));
 }
 
 // ------------------------------------------------------------- XOR compat ---

@@ -220,4 +220,97 @@ int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t
   return check_launch("bhtd_unpack_kernel");
 }
 
+// ------------------------------------------------- pool rows by slot index --
+// The KV pool of an attention backend is [slots, planes, ...] (for SGLang's
+// FlashInfer pool: planes K and V). One extend call's delta KV is the rows of
+// its slot list; the reference copies them out with two fancy-index gathers,
+// after a device-to-host read of the active count (bench_ghostserve_rdp.py:
+// 449-458). slots_gather writes plane p's rows, in slot-list order, to
+// dst[p*n*row_bytes ...] in one pass (a slot < 0 gives a zero row, so no count
+// is needed on the host); slots_scatter writes such a buffer back into the pool
+// (rows of slots < 0 are skipped). A slot >= pool_rows is an error: the row is
+// zeroed (gather) or skipped (scatter) and bit 0 of the layout status is set.
+static __device__ unsigned g_layout_status;
+
+namespace {
+template <typename I>
+__global__ void slots_gather_vec(const char* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
+                                 const I* slots, int64_t n, int64_t pool_rows, char* dst) {
+  const int64_t vpr = row_bytes >> 4;
+  const int64_t total = vpr * n * nplanes;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pr = v / vpr;  // plane * n + list position
+    const int64_t x = (v - pr * vpr) << 4;
+    const int64_t p = pr / n, i = pr - p * n;
+    const int64_t slot = (int64_t)slots[i];
+    uint4 val = vzero();
+    if (slot >= pool_rows) {
+      if (x == 0) atomicOr(&g_layout_status, 1u);
+    } else if (slot >= 0) {
+      val = ldv(pool + slot * pitch + p * plane + x);
+    }
+    stv(dst + pr * row_bytes + x, val);
+  }
+}
+
+template <typename I>
+__global__ void slots_scatter_vec(char* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
+                                  const I* slots, int64_t n, int64_t pool_rows, const char* src) {
+  const int64_t vpr = row_bytes >> 4;
+  const int64_t total = vpr * n * nplanes;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pr = v / vpr;
+    const int64_t x = (v - pr * vpr) << 4;
+    const int64_t p = pr / n, i = pr - p * n;
+    const int64_t slot = (int64_t)slots[i];
+    if (slot >= pool_rows) {
+      if (x == 0) atomicOr(&g_layout_status, 1u);
+    } else if (slot >= 0) {
+      stv(pool + slot * pitch + p * plane + x, ldv(src + pr * row_bytes + x));
+    }
+  }
+}
+}  // namespace
+
+unsigned layout_device_status(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_layout_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_layout_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+int slots_move(bool gather, void* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
+               const void* slots, int slot_bytes, int64_t n, int64_t pool_rows, void* buf, cudaStream_t s) {
+  if (n == 0) return GSEC_OK;
+  if (!aligned16(pool) || !aligned16(buf) || (pitch & 15) || (plane & 15) || (row_bytes & 15) || row_bytes <= 0) {
+    set_error("slot rows: pool, buffer, pitch, plane offset and row bytes must be 16-byte aligned");
+    return GSEC_EINVAL;
+  }
+  const int threads = 256;
+  const int grid = grid_cap((row_bytes >> 4) * n * nplanes, threads);
+  if (gather) {
+    if (slot_bytes == 8)
+      slots_gather_vec<<<grid, threads, 0, s>>>(static_cast<const char*>(pool), pitch, plane, nplanes, row_bytes,
+                                                static_cast<const int64_t*>(slots), n, pool_rows,
+                                                static_cast<char*>(buf));
+    else
+      slots_gather_vec<<<grid, threads, 0, s>>>(static_cast<const char*>(pool), pitch, plane, nplanes, row_bytes,
+                                                static_cast<const int32_t*>(slots), n, pool_rows,
+                                                static_cast<char*>(buf));
+    return check_launch("slots_gather_vec");
+  }
+  if (slot_bytes == 8)
+    slots_scatter_vec<<<grid, threads, 0, s>>>(static_cast<char*>(pool), pitch, plane, nplanes, row_bytes,
+                                               static_cast<const int64_t*>(slots), n, pool_rows,
+                                               static_cast<const char*>(buf));
+  else
+    slots_scatter_vec<<<grid, threads, 0, s>>>(static_cast<char*>(pool), pitch, plane, nplanes, row_bytes,
+                                               static_cast<const int32_t*>(slots), n, pool_rows,
+                                               static_cast<const char*>(buf));
+  return check_launch("slots_scatter_vec");
+}
+
 }  // namespace gsec

@@ -12,13 +12,15 @@ mode="reference"  the reference flow, bit for bit: chunk id from rank 0
                   rotating destination rank (:303-332), fp16 value cast, pack,
                   mod-S row/diagonal parity and a copy of P and Q to the host
                   (:334-392) — with libgsec's kernels instead of the JIT ones.
-mode="fused"      the B200 path: every rank stages its delta KV in a buffer the
-                  other ranks have mapped (CUDA IPC); after one stream-ordered
-                  barrier each rank encodes its 1/world slice of the stripes,
-                  reading all ranks' KV with NVLink peer loads inside the encode
-                  kernel, and offloads its parity slice to pinned host memory
-                  asynchronously.  No gather, no value cast (raw KV bytes), no
-                  host sync besides the active-slot count.
+mode="fused"      the B200 path: every rank gathers its delta KV out of the
+                  pool through the slot list (one kernel per plane, a -1 slot is
+                  a zero row) into a buffer the other ranks have mapped (CUDA
+                  IPC); after one stream-ordered barrier each rank encodes its
+                  1/world slice of the stripes, reading all ranks' KV with NVLink
+                  peer loads inside the encode kernel, and offloads its parity
+                  slice to pinned host memory asynchronously, where it stays
+                  for recover_pool / recover_parts.  No NCCL data gather, no
+                  value cast (raw KV bytes), no host sync.
 
 Both modes append the reference's JSONL record (:377-389) to FT_METRICS_FILE.
 """
@@ -61,7 +63,7 @@ class HookConfig:
     broadcast_chunk_id: bool = True     # reference mode: rank-0 counter + broadcast (:287-301)
     offload: bool = True                # copy parity to pinned host memory
     host_keep: int = 256                # chunks whose parity slice stays in pinned host memory
-    host_budget: int = 1 << 30          # bytes of pinned host memory for that store (at least 4 chunks)
+    host_budget: int = 1 << 30          # bytes of the pinned ring holding them (at least 4 chunks' worth)
     verbose: bool = False
 
 
@@ -77,9 +79,9 @@ class KVFaultTolerance:
         self._staging = None      # fused mode: registered KV staging (2 slots)
         self._peers = None
         self._parity = None
-        self._host_block = None   # one pinned block, sliced into per-chunk parity slots
-        self._slot_bytes = 0
-        self._free_slots = []
+        self._host_block = None   # pinned ring of parity slices (see _host_alloc)
+        self._host_gen = 0
+        self._host_head = 0
         self._store = OrderedDict()  # chunk id -> parity slice record (oldest first)
         self._pending = []        # (record, event, t_enqueue) awaiting D2H completion
         self._copy_stream = None
@@ -217,7 +219,7 @@ class KVFaultTolerance:
                 off += n
 
     def recover_parts(self, chunk_id: int, lost, parts_k, parts_v):
-        """Rebuild the KV shard of chunk `chunk_id` on the lost ranks (at most two).
+        """Rebuild the KV shard of chunk `chunk_id` on the lost ranks (at most m).
 
         Collective over the group, replacement ranks included. Surviving ranks
         pass their chunk's K and V parts (as at encode time) and re-stage them;
@@ -228,6 +230,29 @@ class KVFaultTolerance:
         staging into `parts_k` / `parts_v`. The host parity store is assumed to
         outlive a lost GPU (node memory); a parity slice is only recoverable while
         its chunk is still in the store."""
+        half = sum(t.numel() * t.element_size() for t in parts_k)
+        self._recover_staged(chunk_id, lost, half, parts_k[0].device,
+                             lambda slot: self._stage(slot, half, parts_k, parts_v),
+                             lambda slot: self._unstage(slot, parts_k, parts_v))
+
+    def recover_pool(self, chunk_id: int, lost, kv_pool: torch.Tensor, slots: torch.Tensor):
+        """recover_parts for a chunk encoded by encode_pool: survivors gather the
+        slot list's rows again, the lost ranks' rebuilt rows are scattered back
+        into their pool at the same slots (rows of negative slots untouched)."""
+        row = kv_pool[0, 0].numel() * kv_pool.element_size()
+        half = slots.numel() * row
+
+        def stage(slot):
+            codec.slots_gather(kv_pool, slots, self._staging[slot][0], plane=0)
+            codec.slots_gather(kv_pool, slots, self._staging[slot][1], plane=1)
+
+        def unstage(slot):
+            codec.slots_scatter(kv_pool, slots, self._staging[slot][0], plane=0)
+            codec.slots_scatter(kv_pool, slots, self._staging[slot][1], plane=1)
+
+        self._recover_staged(chunk_id, lost, half, kv_pool.device, stage, unstage)
+
+    def _recover_staged(self, chunk_id, lost, half, device, stage, unstage):
         rank, world = self._rank_world()
         lost = sorted(set(int(r) for r in lost))
         if not lost:
@@ -235,21 +260,20 @@ class KVFaultTolerance:
         entry = self._store.get(chunk_id)
         if entry is None:
             raise KeyError(f"parity of chunk {chunk_id} is no longer in the host store")
-        spec, half, lo, hi = entry["spec"], entry["half"], entry["lo"], entry["hi"]
+        spec, lo, hi = entry["spec"], entry["lo"], entry["hi"]
         if len(lost) > spec.m:
             raise ValueError(f"{len(lost)} lost ranks exceed the code's {spec.m} parity shards")
-        device = parts_k[0].device
-        if sum(t.numel() * t.element_size() for t in parts_k) != half:
-            raise ValueError("parts do not match the encoded chunk size")
+        if half != entry["half"]:
+            raise ValueError("the chunk's KV does not match the encoded chunk size")
         slot = self._calls % 2
         self._calls += 1
         if rank not in lost:
-            self._stage(slot, half, parts_k, parts_v)
+            stage(slot)
         if hi > lo:
+            par = self._parity_bufs(hi - lo, spec.m, device)[slot]
             if self._parity_free[slot] is not None:
                 torch.cuda.current_stream(device).wait_event(self._parity_free[slot])
             torch.cuda.current_stream(device).wait_event(entry["copied"])
-            par = self._parity[slot]
             n = hi - lo
             for j in range(spec.m):
                 par[j][:n].copy_(entry["host"][j * n:(j + 1) * n], non_blocking=True)
@@ -260,7 +284,7 @@ class KVFaultTolerance:
             codec.decode_ptrs(spec, shard_lo, shard_hi, half, 2 * half, lost, lo, hi)
         self._barrier(device)  # every slice of the lost shards has landed
         if rank in lost:
-            self._unstage(slot, parts_k, parts_v)
+            unstage(slot)
 
     def encode_chunk(self, local_k: torch.Tensor, local_v: torch.Tensor, chunk_id: int):
         """Fused P2P encode of this rank's slice; returns the device parity slices."""
@@ -271,9 +295,6 @@ class KVFaultTolerance:
         K and V in every layer of a layer-major cache): the parts are copied once,
         in order, into this rank's peer-mapped staging buffer (K parts, then V
         parts), and the fused encode reads every rank's staging in place."""
-        from . import p2p
-
-        rank, world = self._rank_world()
         device = parts_k[0].device
         half = sum(t.numel() * t.element_size() for t in parts_k)
         if half % 16 or sum(t.numel() * t.element_size() for t in parts_v) != half:
@@ -282,6 +303,46 @@ class KVFaultTolerance:
         slot = self._calls % 2
         self._calls += 1
         self._stage(slot, half, parts_k, parts_v)
+        return self._encode_staged(slot, half, chunk_id, device)
+
+    def encode_pool(self, kv_pool: torch.Tensor, slots: torch.Tensor, chunk_id: int):
+        """encode_chunk of one extend call's delta KV read straight out of the KV
+        pool [slots, 2 (K, V), heads, head_dim] through its slot list: one
+        gather kernel per plane writes the rows into the staging buffer (a
+        negative slot is a zero row), so neither the active count nor the
+        gathered K/V ever reaches the host (bench_ghostserve_rdp.py:449-458 reads
+        the count back and copies the rows twice). Every rank of the group must
+        pass a slot list of the same length (tensor-parallel ranks share it)."""
+        device = kv_pool.device
+        row = kv_pool[0, 0].numel() * kv_pool.element_size()
+        half = slots.numel() * row
+        if half % 16:
+            raise ValueError("pool rows must be multiples of 16 bytes")
+        self._ensure_staging(half, device)
+        slot = self._calls % 2
+        self._calls += 1
+        codec.slots_gather(kv_pool, slots, self._staging[slot][0], plane=0)
+        codec.slots_gather(kv_pool, slots, self._staging[slot][1], plane=1)
+        return self._encode_staged(slot, half, chunk_id, device)
+
+    def _parity_bufs(self, nbytes: int, m: int, device):
+        """The two device parity slots (m buffers each) with room for nbytes."""
+        if self._parity is None or len(self._parity[0]) != m or self._parity[0][0].numel() < max(nbytes, 16):
+            if self._parity is not None:
+                for ev in self._parity_free:  # host copies still reading the old buffers
+                    if ev is not None:
+                        ev.synchronize()
+            self._parity = [[torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device) for _ in range(m)]
+                            for _ in range(2)]
+            self._parity_free = [None, None]
+        return self._parity
+
+    def _encode_staged(self, slot: int, half: int, chunk_id: int, device):
+        """Encode this rank's stripe slice of the codeword whose data shards are
+        every rank's staging slot `slot` (K ++ V, half bytes each)."""
+        from . import p2p
+
+        rank, world = self._rank_world()
         self._barrier(device)  # every rank's staging write precedes every peer read
         spec = self._spec(world)
         data_bytes = 2 * half
@@ -291,13 +352,9 @@ class KVFaultTolerance:
         lo, hi = lo * g, hi * g
         # parity buffers alternate with the staging slot; before overwriting one,
         # wait only for the host copy that last read it (not for the copy stream)
-        if self._parity is None or self._parity[0][0].numel() < max(hi - lo, 16):
-            self._parity = [[torch.empty(max(hi - lo, 16), dtype=torch.uint8, device=device) for _ in range(spec.m)]
-                            for _ in range(2)]
-            self._parity_free = [None, None]
+        parity = self._parity_bufs(hi - lo, spec.m, device)[slot]
         if self._parity_free[slot] is not None:
             torch.cuda.current_stream(device).wait_event(self._parity_free[slot])
-        parity = self._parity[slot]
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -318,20 +375,30 @@ class KVFaultTolerance:
         self._drain(block=False)
         return [t[:hi - lo] for t in parity], (lo, hi)
 
-    def _host_slot(self, nbytes: int):
-        """A pinned host slot for one chunk's parity slice. The store is one pinned
-        block allocated on first use (pinning is slow) and recycled oldest-first."""
-        if self._host_block is None or self._slot_bytes < nbytes:
-            keep = max(4, min(self.cfg.host_keep, self.cfg.host_budget // max(nbytes, 1)))
-            self._host_block = torch.empty(keep * nbytes, dtype=torch.uint8, pin_memory=True)
-            self._slot_bytes = nbytes
-            self._free_slots = list(range(keep - 1, -1, -1))
-            self._store.clear()
-        if not self._free_slots:
-            _, old = self._store.popitem(last=False)
-            self._free_slots.append(old["slot"])
-        slot = self._free_slots.pop()
-        return slot, self._host_block[slot * self._slot_bytes: slot * self._slot_bytes + nbytes]
+    def _host_alloc(self, nbytes: int):
+        """Pinned host bytes for one chunk's parity slice.
+
+        The store is a ring over one pinned block (pinning is slow, so it is
+        allocated once and only replaced by a larger one when a chunk does not
+        fit): chunks take consecutive byte ranges, wrapping at the end, and the
+        chunks whose bytes a new one overwrites are dropped (they are the oldest
+        in the block). At most host_keep chunks are kept. Chunks stored in a
+        replaced block stay readable until they are dropped by count."""
+        if self._host_block is None or nbytes > self._host_block.numel():
+            size = max(4 * nbytes, min(self.cfg.host_budget, self.cfg.host_keep * nbytes))
+            self._host_block = torch.empty(size, dtype=torch.uint8, pin_memory=True)
+            self._host_gen += 1
+            self._host_head = 0
+        if self._host_head + nbytes > self._host_block.numel():
+            self._host_head = 0
+        lo, hi = self._host_head, self._host_head + nbytes
+        for cid in [c for c, e in self._store.items()
+                    if e["gen"] == self._host_gen and e["off"] < hi and lo < e["off"] + e["size"]]:
+            del self._store[cid]
+        while len(self._store) >= max(1, self.cfg.host_keep):
+            self._store.popitem(last=False)
+        self._host_head = hi
+        return self._host_block[lo:hi], dict(gen=self._host_gen, off=lo, size=nbytes)
 
     def _offload(self, rec, parity, e0, e1, entry):
         """Copy this rank's parity slice to its pinned host slot on a side stream;
@@ -341,9 +408,10 @@ class KVFaultTolerance:
             self._copy_stream = torch.cuda.Stream(dev)
         nbytes = sum(t.numel() for t in parity)
         old = self._store.pop(rec["chunk_id"], None)
-        if old is not None:  # a chunk id encoded again replaces its earlier parity
-            self._free_slots.append(old["slot"])
-        slot, host = self._host_slot(nbytes)
+        if old is not None and old["gen"] == self._host_gen and old["size"] == nbytes:
+            host, place = old["host"], dict(gen=old["gen"], off=old["off"], size=nbytes)  # encoded again: same bytes
+        else:
+            host, place = self._host_alloc(nbytes)
         self._copy_stream.wait_stream(torch.cuda.current_stream(dev))
         d0 = torch.cuda.Event(enable_timing=True)
         d1 = torch.cuda.Event(enable_timing=True)
@@ -354,7 +422,7 @@ class KVFaultTolerance:
                 host[off:off + t.numel()].copy_(t, non_blocking=True)
                 off += t.numel()
             d1.record()
-        entry.update(slot=slot, host=host, copied=d1)
+        entry.update(place, host=host, copied=d1)
         self._store[rec["chunk_id"]] = entry
         self._pending.append((rec, (d0, d1), e0, e1))
         return d1
@@ -423,6 +491,15 @@ class KVFaultTolerance:
             return
         if not isinstance(slots, torch.Tensor):
             slots = torch.as_tensor(slots, device=kv_pool.device)
+        if self.cfg.mode != "reference":
+            # the pool is read through the slot list on the device: no host sync
+            if slots.numel() == 0:
+                return
+            chunk_id, _ = self.next_chunk_id(device=kv_pool.device)
+            if self.first_chunk_wall_ms is None and self.cfg.prog_start_mono == self.cfg.prog_start_mono:
+                self.first_chunk_wall_ms = (time.perf_counter() - self.cfg.prog_start_mono) * 1000.0
+            self.encode_pool(kv_pool, slots.contiguous(), chunk_id)
+            return
         active = slots != -1
         if int(active.sum().item()) == 0:
             return
@@ -432,12 +509,9 @@ class KVFaultTolerance:
         chunk_id, dst_rank = self.next_chunk_id(device=local_k.device)
         if self.first_chunk_wall_ms is None and self.cfg.prog_start_mono == self.cfg.prog_start_mono:
             self.first_chunk_wall_ms = (time.perf_counter() - self.cfg.prog_start_mono) * 1000.0
-        if self.cfg.mode == "reference":
-            gathered = self.gather_kv(local_k, local_v, dst_rank)
-            if gathered is not None:
-                self.compute_parity_to_cpu(*gathered, chunk_id, dst_rank)
-        else:
-            self.encode_chunk(local_k, local_v, chunk_id)
+        gathered = self.gather_kv(local_k, local_v, dst_rank)
+        if gathered is not None:
+            self.compute_parity_to_cpu(*gathered, chunk_id, dst_rank)
 
 
 def patch_backend(backend, ft: KVFaultTolerance) -> bool:

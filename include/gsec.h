@@ -135,6 +135,25 @@ GSEC_API int gsec_rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes
                      void* dst0, int64_t len0, void* dst1, int64_t len1,
                      gsec_stream_t stream);
 
+/* Gather the rows of a slot list out of a KV pool [pool_rows, nplanes, ...]:
+ * plane p (at byte offset p*plane inside a slot's pitch-byte record) of slot
+ * slots[i] goes to dst + (p*n + i)*row_bytes. A negative slot gives a zero row
+ * (no active count is needed on the host). slot_bytes = 4 or 8 (int32/int64
+ * list). Pool, dst, pitch, plane and row_bytes 16-byte aligned. A slot >=
+ * pool_rows zeroes its row and sets bit 16 of gsec_device_status.
+ * Replaces the delta-KV extraction of the reference hook: the active count
+ * read back to the host and kv_pool[active_slots, 0/1].contiguous()
+ * (bench_ghostserve_rdp.py:449-458). */
+GSEC_API int gsec_slots_gather(const void* pool, int64_t pitch, int64_t plane, int32_t nplanes,
+                      int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n,
+                      int64_t pool_rows, void* dst, gsec_stream_t stream);
+/* Inverse of gsec_slots_gather: src's rows back into the pool (rows of
+ * negative slots are skipped). Used to restore a rebuilt delta into a
+ * replacement rank's pool; the reference has no restore path. */
+GSEC_API int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_t nplanes,
+                       int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n,
+                       int64_t pool_rows, const void* src, gsec_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* ref-compat: XOR (benchmark/xor/kernel.cu)                                   */
 /* ------------------------------------------------------------------------- */

@@ -207,3 +207,74 @@ def hook_recover(rank, world, port, backend, scheme, lost_sets, out):
     dist.all_gather_object(oks, ok)
     out.put((rank, all(oks), evicted))
     dist.destroy_process_group()
+
+
+def hook_pool(rank, world, port, backend, out):
+    """The hook as SGLang drives it: a FlashInfer-like backend whose KV pool
+    [slots, 2, heads, 128] is read through each extend call's slot_mapping
+    (a permutation with -1 padding). Fused parity must equal the oracle's over
+    the gathered rows (zero rows for -1), and a lost rank's pool rows must come
+    back bit-exact through recover_pool."""
+    _init(rank, world, port, backend)
+    dev = rank if backend == "nccl" else 0
+    torch.cuda.set_device(dev)
+    hook = _pkg("hook")
+    from oracle import codes
+
+    class FlashInferAttnBackend:
+        def __init__(self):
+            g = torch.Generator(device="cuda").manual_seed(100 + rank)
+            self.kv_buffer = torch.randn(512, 2, 2, 128, device="cuda", generator=g).to(torch.bfloat16)
+
+        def forward_extend(self, batch, layer=None, save_kv_cache=True):
+            return "attn-out"
+
+    class Batch:
+        def __init__(self, slot_mapping):
+            self.slot_mapping = slot_mapping
+
+    be = FlashInferAttnBackend()
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme="rdp", unit=1024, metrics_file=None))
+    assert hook.patch_backend(be, ft)
+    gen = torch.Generator().manual_seed(5)  # same slot lists on every rank, as tensor-parallel ranks see
+    calls = []
+    for n, dtype in ((96, torch.int64), (40, torch.int32), (200, torch.int64)):
+        perm = torch.randperm(512, generator=gen)[:n].to(dtype)
+        perm[torch.randperm(n, generator=gen)[: n // 8]] = -1
+        calls.append(perm.cuda())
+    ok = True
+    spec = ft._spec(world)
+    for sm in calls:
+        assert be.forward_extend(Batch(sm), layer=0) == "attn-out"
+        torch.cuda.synchronize()
+        s64 = sm.to(torch.int64)
+        rows = be.kv_buffer[s64.clamp(min=0)].clone()
+        rows[s64 < 0] = 0
+        shard = torch.cat([rows[:, 0].reshape(-1).view(torch.uint8), rows[:, 1].reshape(-1).view(torch.uint8)])
+        shards = [None] * world
+        dist.all_gather_object(shards, shard.cpu().numpy())
+        ft.flush()
+        entry = ft._store[ft.chunk_counter]
+        mine = entry["host"].numpy().copy()
+        got = [None] * world
+        dist.all_gather_object(got, (entry["lo"], entry["hi"], mine))
+        if rank == 0:
+            want = codes.rdp_encode(list(shards), spec.p, spec.unit)
+            for j in range(2):
+                parts = [g[2][j * (g[1] - g[0]):(j + 1) * (g[1] - g[0])] for g in got]
+                ok = ok and np.array_equal(np.concatenate(parts), want[j])
+    # lose rank 1 (and both ranks) and rebuild every call's rows in the pool
+    for lost in ([1], [0, 1]):
+        saved = be.kv_buffer.clone()
+        for cid, sm in enumerate(calls, start=1):
+            if rank in lost:
+                s64 = sm.to(torch.int64)
+                be.kv_buffer[s64[s64 >= 0]] = 0
+            ft.recover_pool(cid, lost, be.kv_buffer, sm)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(be.kv_buffer, saved)
+    ft.close()
+    oks = [None] * world
+    dist.all_gather_object(oks, ok)
+    out.put((rank, all(oks), [r["chunk_id"] for r in ft.records]))
+    dist.destroy_process_group()

@@ -242,3 +242,53 @@ def test_config0_xor_full_size():
     full = data + par
     out = g.decode(spec, [None if i == e else full[i] for i in range(8)], [e], data_bytes=32 << 20)
     assert torch.equal(out[e], full[e])
+
+
+# ------------------------------------------------------- pool rows by slot ---
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+@pytest.mark.parametrize("heads", [1, 2, 8])
+def test_slots_gather_scatter_match_fancy_indexing(dtype, heads):
+    codec = pkg("codec")
+    pool = torch.randn(1000, 2, heads, 128, device="cuda").to(torch.bfloat16)
+    slots = torch.randperm(1000, device="cuda")[:333].to(dtype)
+    slots[::7] = -1
+    row = heads * 128 * 2
+    for plane in (0, 1):
+        out = torch.empty(333 * row + 64, dtype=torch.uint8, device="cuda")
+        codec.slots_gather(pool, slots, out, plane=plane)
+        want = pool[slots.long().clamp(min=0), plane].clone()
+        want[slots.long() < 0] = 0
+        assert torch.equal(out[:333 * row], want.reshape(-1).view(torch.uint8))
+    # scatter puts rows back exactly where gather took them; -1 rows untouched
+    src = torch.randint(0, 256, (333 * row,), dtype=torch.uint8, device="cuda")
+    before = pool.clone()
+    codec.slots_scatter(pool, slots, src, plane=1)
+    s = slots.long()
+    expect = before.clone()
+    expect[s[s >= 0], 1] = src.view(torch.bfloat16).view(333, heads, 128)[s >= 0]
+    assert torch.equal(pool.view(torch.int16), expect.view(torch.int16))  # random bytes include NaNs
+
+
+def test_slots_gather_flags_a_slot_past_the_pool():
+    codec = pkg("codec")
+    pool = torch.zeros(64, 2, 1, 128, device="cuda", dtype=torch.bfloat16)
+    slots = torch.tensor([3, 64, 5], device="cuda")
+    out = torch.full((3 * 256,), 7, dtype=torch.uint8, device="cuda")
+    codec.slots_gather(pool, slots, out)
+    assert codec.device_status(clear=True) == 1 << 16
+    assert int(out[256:512].sum()) == 0  # the bad row is zeroed, not read
+
+
+def test_slots_gather_rejects_bad_arguments():
+    codec = pkg("codec")
+    pool = torch.zeros(64, 2, 1, 128, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(4096, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError):
+        codec.slots_gather(pool, torch.tensor([1, 2], device="cuda", dtype=torch.int16), out)
+    with pytest.raises(ValueError):
+        codec.slots_gather(pool, torch.arange(40, device="cuda"), out[:100])
+    with pytest.raises(ValueError):
+        wide = torch.zeros(64, 2, 2, 128, device="cuda", dtype=torch.bfloat16)
+        codec.slots_gather(wide[:, :, :, :64], torch.arange(4, device="cuda"), out)  # rows not contiguous
+    with pytest.raises(ValueError):
+        codec.slots_gather(pool, torch.arange(4, device="cuda"), out[1:])  # misaligned buffer

@@ -28,3 +28,10 @@ def test_hook_recover_lost_ranks_two_gpus(scheme, lost_sets):
     for _rank, ok, evicted in res:
         assert ok is True
         assert evicted is True
+
+
+def test_hook_reads_kv_pool_through_slot_mapping_two_gpus():
+    res = run_ranks(mp_workers.hook_pool, 2, "nccl", timeout=300)
+    for _rank, ok, recs in res:
+        assert ok is True
+        assert recs == [1, 2, 3]

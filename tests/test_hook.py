@@ -29,8 +29,17 @@ def run_ranks(fn, world, *args, timeout=120):
         p.start()
     res = []
     try:
-        for _ in procs:
-            res.append(q.get(timeout=timeout))
+        import queue as _queue
+        import time as _time
+        deadline = _time.monotonic() + timeout
+        while len(res) < len(procs):
+            try:
+                res.append(q.get(timeout=1.0))
+            except _queue.Empty:
+                # a rank that died leaves the others waiting on it: fail now
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                assert not dead, f"a rank exited with {dead}"
+                assert _time.monotonic() < deadline, "ranks timed out"
     finally:
         for p in procs:
             p.join(timeout=30)
