@@ -469,6 +469,15 @@ int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_t nplanes
                     const_cast<void*>(src), as_stream(stream));
 }
 
+int gsec_copy_async(void* dst, const void* src, int64_t bytes, gsec_stream_t stream) {
+  GSEC_REQUIRE(bytes >= 0, "bytes < 0");
+  if (bytes == 0) return GSEC_OK;
+  GSEC_REQUIRE(dst != nullptr && src != nullptr, "null pointer");
+  if (cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, as_stream(stream)) != cudaSuccess)
+    return check_launch("cudaMemcpyAsync");
+  return GSEC_OK;
+}
+
 // ------------------------------------------------------------- XOR compat ---
 namespace {
 // Row r of a row-major shard buffer as a contiguous LinearPass input/output.

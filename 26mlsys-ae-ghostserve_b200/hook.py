@@ -30,14 +30,14 @@ import functools
 import json
 import os
 import time
-from collections import OrderedDict
+from collections import OrderedDict, deque
 from dataclasses import dataclass, field
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
-from . import codec, ext
+from . import _lib, codec, ext
 
 ENV_FLAG = "SGLANG_GATHER_KV_TO_GPU0"
 LOG_PREFIX = "[ft-rdp]"
@@ -87,6 +87,11 @@ class KVFaultTolerance:
         self._copy_stream = None
         self._parity_free = [None, None]
         self._calls = 0
+        self._bar_t = None        # the barrier's all-reduce operand
+        self._plans = {}          # (slot, half, stream) -> marshalled encode of that staging slot
+        self._pools = {}          # KV pool geometry by (pointer, shape, strides)
+        self._events = []         # timing events free for reuse
+        self._ring = deque()      # entries of the current pinned block in ring order
 
     # ------------------------------------------------------------- control --
     def _rank_world(self):
@@ -112,8 +117,9 @@ class KVFaultTolerance:
     def _barrier(self, device):
         """Stream-ordered on NCCL (a 1-element all-reduce); host-side otherwise."""
         if dist.get_backend(self.group) == "nccl":
-            t = torch.zeros(1, device=device)
-            dist.all_reduce(t, group=self.group)
+            if self._bar_t is None or self._bar_t.device != torch.device(device):
+                self._bar_t = torch.zeros(1, device=device)
+            dist.all_reduce(self._bar_t, group=self.group)
         else:
             torch.cuda.current_stream(device).synchronize()
             dist.barrier(group=self.group)
@@ -194,6 +200,7 @@ class KVFaultTolerance:
         cap = -(-cap // 4096) * 4096
         # two slots, each a K buffer and a V buffer; peers read them in place
         self._staging = [[torch.empty(cap, dtype=torch.uint8, device=device) for _ in range(2)] for _ in range(2)]
+        self._plans.clear()
         flat = [t for slot in self._staging for t in slot]
         self._peers = p2p.PeerGroup.create(flat, group=self.group)
 
@@ -239,18 +246,11 @@ class KVFaultTolerance:
         """recover_parts for a chunk encoded by encode_pool: survivors gather the
         slot list's rows again, the lost ranks' rebuilt rows are scattered back
         into their pool at the same slots (rows of negative slots untouched)."""
-        row = kv_pool[0, 0].numel() * kv_pool.element_size()
-        half = slots.numel() * row
-
-        def stage(slot):
-            codec.slots_gather(kv_pool, slots, self._staging[slot][0], plane=0)
-            codec.slots_gather(kv_pool, slots, self._staging[slot][1], plane=1)
-
-        def unstage(slot):
-            codec.slots_scatter(kv_pool, slots, self._staging[slot][0], plane=0)
-            codec.slots_scatter(kv_pool, slots, self._staging[slot][1], plane=1)
-
-        self._recover_staged(chunk_id, lost, half, kv_pool.device, stage, unstage)
+        geo = self._pool_geometry(kv_pool)
+        half = slots.numel() * geo[0]
+        self._recover_staged(chunk_id, lost, half, kv_pool.device,
+                             lambda slot: self._gather_pool(kv_pool, geo, slots, slot, True),
+                             lambda slot: self._gather_pool(kv_pool, geo, slots, slot, False))
 
     def _recover_staged(self, chunk_id, lost, half, device, stage, unstage):
         rank, world = self._rank_world()
@@ -314,16 +314,38 @@ class KVFaultTolerance:
         the count back and copies the rows twice). Every rank of the group must
         pass a slot list of the same length (tensor-parallel ranks share it)."""
         device = kv_pool.device
-        row = kv_pool[0, 0].numel() * kv_pool.element_size()
-        half = slots.numel() * row
+        geo = self._pool_geometry(kv_pool)
+        half = slots.numel() * geo[0]
         if half % 16:
             raise ValueError("pool rows must be multiples of 16 bytes")
         self._ensure_staging(half, device)
         slot = self._calls % 2
         self._calls += 1
-        codec.slots_gather(kv_pool, slots, self._staging[slot][0], plane=0)
-        codec.slots_gather(kv_pool, slots, self._staging[slot][1], plane=1)
+        self._gather_pool(kv_pool, geo, slots, slot, True)
         return self._encode_staged(slot, half, chunk_id, device)
+
+    def _pool_geometry(self, kv_pool):
+        """(row bytes, slot pitch, V plane offset) of the pool, checked once per pool."""
+        key = (kv_pool.data_ptr(), tuple(kv_pool.shape), tuple(kv_pool.stride()), kv_pool.dtype)
+        geo = self._pools.get(key)
+        if geo is None:
+            row, pitch, _ = codec._pool_geometry(kv_pool, 0)
+            _, _, voff = codec._pool_geometry(kv_pool, 1)
+            geo = self._pools[key] = (row, pitch, voff)
+        return geo
+
+    def _gather_pool(self, kv_pool, geo, slots, slot, gather: bool):
+        """K and V planes of the slot list's rows into (gather) or out of
+        (scatter) staging slot `slot`: two gsec_slots_* calls."""
+        if slots.dtype not in (torch.int32, torch.int64) or not slots.is_contiguous() or \
+                slots.device != kv_pool.device:
+            raise ValueError("slots must be a contiguous int32/int64 tensor on the pool's device")
+        row, pitch, voff = geo
+        fn = _lib.lib().gsec_slots_gather if gather else _lib.lib().gsec_slots_scatter
+        base, sp, n, es = kv_pool.data_ptr(), slots.data_ptr(), slots.numel(), slots.element_size()
+        stream = torch.cuda.current_stream(kv_pool.device).cuda_stream
+        for plane_off, buf in ((0, self._staging[slot][0]), (voff, self._staging[slot][1])):
+            _lib.check(fn(base + plane_off, pitch, 0, 1, row, sp, es, n, kv_pool.shape[0], buf.data_ptr(), stream))
 
     def _parity_bufs(self, nbytes: int, m: int, device):
         """The two device parity slots (m buffers each) with room for nbytes."""
@@ -335,45 +357,61 @@ class KVFaultTolerance:
             self._parity = [[torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device) for _ in range(m)]
                             for _ in range(2)]
             self._parity_free = [None, None]
+            self._plans.clear()
         return self._parity
+
+    def _plan(self, slot: int, half: int, device):
+        """Stripe slice, parity views and the marshalled encode of staging slot
+        `slot` holding half-byte K and V halves (built once per shape)."""
+        from . import p2p
+
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (slot, half, stream)
+        plan = self._plans.get(key)
+        if plan is None:
+            rank, world = self._rank_world()
+            spec = self._spec(world)
+            data_bytes = 2 * half
+            g = spec.stripe_bytes()
+            lo, hi = p2p.stripe_slice(rank, world, spec.parity_bytes(data_bytes) // g)
+            lo, hi = lo * g, hi * g
+            parity = self._parity_bufs(hi - lo, spec.m, device)[slot]
+            enc = None
+            if hi > lo:
+                enc = codec.PreparedEncode(spec, [self._peers.ptr(r, 2 * slot) for r in range(world)],
+                                           [self._peers.ptr(r, 2 * slot + 1) for r in range(world)], half,
+                                           data_bytes, [t.data_ptr() - lo for t in parity], lo, hi, stream)
+            plan = self._plans[key] = dict(spec=spec, lo=lo, hi=hi, enc=enc, views=[t[:hi - lo] for t in parity])
+        return plan
+
+    def _event(self):
+        return self._events.pop() if self._events else torch.cuda.Event(enable_timing=True)
 
     def _encode_staged(self, slot: int, half: int, chunk_id: int, device):
         """Encode this rank's stripe slice of the codeword whose data shards are
         every rank's staging slot `slot` (K ++ V, half bytes each)."""
-        from . import p2p
-
-        rank, world = self._rank_world()
         self._barrier(device)  # every rank's staging write precedes every peer read
-        spec = self._spec(world)
-        data_bytes = 2 * half
-        pbytes = spec.parity_bytes(data_bytes)
-        g = spec.stripe_bytes()
-        lo, hi = p2p.stripe_slice(rank, world, pbytes // g)
-        lo, hi = lo * g, hi * g
+        plan = self._plan(slot, half, device)
+        spec, lo, hi = plan["spec"], plan["lo"], plan["hi"]
         # parity buffers alternate with the staging slot; before overwriting one,
         # wait only for the host copy that last read it (not for the copy stream)
-        parity = self._parity_bufs(hi - lo, spec.m, device)[slot]
         if self._parity_free[slot] is not None:
             torch.cuda.current_stream(device).wait_event(self._parity_free[slot])
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
+        e0, e1 = self._event(), self._event()
         e0.record()
-        if hi > lo:
-            data_lo = [self._peers.ptr(r, 2 * slot) for r in range(world)]
-            data_hi = [self._peers.ptr(r, 2 * slot + 1) for r in range(world)]
-            codec.encode_ptrs(spec, data_lo, data_hi, half, data_bytes,
-                              [t.data_ptr() - lo for t in parity], lo, hi)
+        if plan["enc"] is not None:
+            plan["enc"]()
         e1.record()
         rec = self._record(chunk_id, -1, None, None, None, spec.m * (hi - lo))
         rec["slice"] = [lo, hi]
         rec["scheme"] = spec.scheme
         if self.cfg.offload and hi > lo:
             entry = dict(lo=lo, hi=hi, half=half, spec=spec)
-            self._parity_free[slot] = self._offload(rec, [t[:hi - lo] for t in parity], e0, e1, entry)
+            self._parity_free[slot] = self._offload(rec, plan["views"], e0, e1, entry)
         else:
             self._pending.append((rec, None, e0, e1))
         self._drain(block=False)
-        return [t[:hi - lo] for t in parity], (lo, hi)
+        return plan["views"], (lo, hi)
 
     def _host_alloc(self, nbytes: int):
         """Pinned host bytes for one chunk's parity slice.
@@ -385,16 +423,23 @@ class KVFaultTolerance:
         in the block). At most host_keep chunks are kept. Chunks stored in a
         replaced block stay readable until they are dropped by count."""
         if self._host_block is None or nbytes > self._host_block.numel():
+            if self._copy_stream is not None:
+                # the block's bytes are written by raw copies the allocator does not
+                # track: let them land before the block can be released
+                self._copy_stream.synchronize()
             size = max(4 * nbytes, min(self.cfg.host_budget, self.cfg.host_keep * nbytes))
             self._host_block = torch.empty(size, dtype=torch.uint8, pin_memory=True)
             self._host_gen += 1
             self._host_head = 0
+            self._ring.clear()
         if self._host_head + nbytes > self._host_block.numel():
             self._host_head = 0
         lo, hi = self._host_head, self._host_head + nbytes
-        for cid in [c for c, e in self._store.items()
-                    if e["gen"] == self._host_gen and e["off"] < hi and lo < e["off"] + e["size"]]:
-            del self._store[cid]
+        # this block's entries sit in ring order: the ones the new bytes overwrite are at the front
+        while self._ring and self._ring[0]["off"] < hi and lo < self._ring[0]["off"] + self._ring[0]["size"]:
+            old = self._ring.popleft()
+            if self._store.get(old["cid"]) is old:
+                del self._store[old["cid"]]
         while len(self._store) >= max(1, self.cfg.host_keep):
             self._store.popitem(last=False)
         self._host_head = hi
@@ -412,17 +457,24 @@ class KVFaultTolerance:
             host, place = old["host"], dict(gen=old["gen"], off=old["off"], size=nbytes)  # encoded again: same bytes
         else:
             host, place = self._host_alloc(nbytes)
-        self._copy_stream.wait_stream(torch.cuda.current_stream(dev))
-        d0 = torch.cuda.Event(enable_timing=True)
-        d1 = torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(self._copy_stream):
-            d0.record()
-            off = 0
-            for t in parity:
-                host[off:off + t.numel()].copy_(t, non_blocking=True)
-                off += t.numel()
-            d1.record()
-        entry.update(place, host=host, copied=d1)
+        cs = self._copy_stream
+        ready = self._event()
+        ready.record(torch.cuda.current_stream(dev))
+        cs.wait_event(ready)
+        self._events.append(ready)  # a later record does not change the wait already enqueued
+        d0 = self._event()
+        d1 = torch.cuda.Event(enable_timing=True)  # kept by the store entry: not pooled
+        d0.record(cs)
+        dst, copy = host.data_ptr(), _lib.lib().gsec_copy_async
+        for t in parity:  # raw stream-ordered copies: no per-copy framework bookkeeping
+            _lib.check(copy(dst, t.data_ptr(), t.numel(), cs.cuda_stream))
+            dst += t.numel()
+        d1.record(cs)
+        entry.update(place, host=host, copied=d1, cid=rec["chunk_id"])
+        if old is None or entry["off"] != old["off"] or entry["gen"] != old["gen"]:
+            self._ring.append(entry)
+        else:  # same bytes as before: the ring keeps the earlier entry's place
+            self._ring = deque(entry if e is old else e for e in self._ring)
         self._store[rec["chunk_id"]] = entry
         self._pending.append((rec, (d0, d1), e0, e1))
         return d1
@@ -442,6 +494,8 @@ class KVFaultTolerance:
                     continue
                 d2h[1].synchronize()
                 rec["timings"]["gpu_to_cpu_ms"] = float(d2h[0].elapsed_time(d2h[1]))
+                self._events.append(d2h[0])
+            self._events += [e0, e1]
             self._emit(rec)
         self._pending = keep
 

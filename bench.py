@@ -228,7 +228,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill"])
+    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill", "hook"])
+    ap.add_argument("--hook-tokens", type=int, default=2048, help="hook workload: tokens per extend call")
+    ap.add_argument("--hook-modes", default="fused,reference", help="hook workload: modes to time")
     ap.add_argument("--prefill-seqs", type=int, default=16)
     ap.add_argument("--prefill-len", type=int, default=32768)
     ap.add_argument("--prefill-chunk", type=int, default=2048)
@@ -245,6 +247,9 @@ def main():
     args = ap.parse_args()
     if args.workload == "prefill":
         run_prefill_bench(args)
+        return
+    if args.workload == "hook":
+        run_hook_bench(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -404,11 +409,9 @@ def verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device):
     return all(torch.equal(a, b) for a, b in zip(again, parity)) and g.codec.device_status(clear=True) == 0
 
 
-def run_prefill_bench(args):
-    """Config 3: TP prefill of a Llama-3.1-8B-architecture model (random bf16
-    weights), prefill tokens/s without parity and with it (fused / reference)."""
+def init_nccl():
+    """One rank per GPU over NCCL (also at N=1, so the hook's collectives exist)."""
     import datetime
-    import importlib
     import socket
 
     import torch
@@ -429,6 +432,109 @@ def run_prefill_bench(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    return world, rank, device
+
+
+def run_hook_bench(args):
+    """The SGLang-side hook per forward_extend call: a FlashInfer-like backend
+    whose KV pool [slots, 2, 8/world heads, 128] bf16 is patched with
+    hook.patch_backend; each step is one prefill chunk of --hook-tokens tokens
+    through --prefill-layers extend calls (one per layer, each with the same
+    shuffled slot list, as the attention backend sees it). Fused mode (pool
+    read through the slot list, P2P sliced encode, async host copy) vs the
+    reference flow (active count to host, fancy-index copies, rank-0 chunk id,
+    NCCL gather to the rotating rank, fp16 cast, mod-S parity, synchronous host
+    copy). Time per call = max over ranks of the CUDA-event time of the steps."""
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, device = init_nccl()
+    hook = importlib.import_module(PKG + ".hook")
+    heads = max(1, 8 // world)
+    pool_slots = 1 << 17
+    T = args.hook_tokens
+
+    class FlashInferAttnBackend:
+        def __init__(self):
+            g = torch.Generator(device=device).manual_seed(rank)
+            self.kv_buffer = torch.randn(pool_slots, 2, heads, 128, device=device, generator=g).to(torch.bfloat16)
+
+        def forward_extend(self, batch, layer=None, save_kv_cache=True):
+            return None
+
+    class Batch:
+        def __init__(self, slot_mapping):
+            self.slot_mapping = slot_mapping
+
+    gen = torch.Generator().manual_seed(3)  # identical slot lists on every rank
+    lists = [torch.randperm(pool_slots, generator=gen)[:T].to(device) for _ in range(4)]
+    out = {}
+    for mode in [m for m in args.hook_modes.split(",") if m]:
+        be = FlashInferAttnBackend()
+        # "fused_device": the fused path with the parity kept in HBM (no host copy)
+        ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused" if mode.startswith("fused") else mode,
+                                                   offload=mode != "fused_device", metrics_file=None))
+        hook.patch_backend(be, ft)
+
+        def step(i):
+            b = Batch(lists[i % len(lists)])
+            for layer in range(args.prefill_layers):
+                be.forward_extend(b, layer=layer)
+
+        for i in range(args.warmup):
+            step(i)
+        ft.flush()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        h0 = time.perf_counter()
+        for i in range(args.steps):
+            step(i)
+        h1 = time.perf_counter()
+        ft.flush()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1), (h1 - h0) * 1e3], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        calls = args.steps * args.prefill_layers
+        ms = float(t[0].item()) / calls
+        kv = 2 * T * heads * 128 * 2 * world  # K and V bytes of one call, all ranks
+        out[mode] = {"us_per_call": round(ms * 1e3, 2), "kv_gb_s": round(kv / (ms * 1e-3) / 1e9, 2),
+                     "host_issue_us_per_call": round(float(t[1].item()) / calls * 1e3, 2),
+                     "records": len(ft.records)}
+        ft.close()
+    if rank == 0:
+        head = "fused" if "fused" in out else next(iter(out))
+        line = {
+            "metric": "KV hook time per forward_extend call (one layer of a prefill chunk)",
+            "value": out[head]["us_per_call"], "unit": "us/call", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic (random KV pool, shuffled slot lists)",
+            "config": {"workload": "hook", "tokens_per_call": T, "kv_heads_per_rank": heads,
+                       "calls_per_step": args.prefill_layers, "pool_slots": pool_slots,
+                       "parity_code": "fused: RDP over the ranks (k = world); reference: mod-S RDP at the "
+                                      "rotating rank"},
+            "modes": out,
+        }
+        if "fused" in out and "reference" in out:
+            line["speedup_vs_reference_flow"] = round(out["reference"]["us_per_call"] / out["fused"]["us_per_call"], 2)
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def run_prefill_bench(args):
+    """Config 3: TP prefill of a Llama-3.1-8B-architecture model (random bf16
+    weights), prefill tokens/s without parity and with it (fused / reference)."""
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, device = init_nccl()
     pre = importlib.import_module(PKG + ".prefill")
     hook = importlib.import_module(PKG + ".hook")
     spec = pre.ModelSpec(layers=args.prefill_layers)

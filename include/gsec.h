@@ -154,6 +154,13 @@ GSEC_API int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_
                        int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n,
                        int64_t pool_rows, const void* src, gsec_stream_t stream);
 
+/* Stream-ordered copy of `bytes` bytes between any two addresses the device
+ * can reach (device, pinned host, mapped peer). The hook offloads each parity
+ * slice with it, one call per parity shard. No reference counterpart (the
+ * reference copies P and Q with a blocking tensor .to("cpu"),
+ * bench_ghostserve_rdp.py:362-366). */
+GSEC_API int gsec_copy_async(void* dst, const void* src, int64_t bytes, gsec_stream_t stream);
+
 /* ------------------------------------------------------------------------- */
 /* ref-compat: XOR (benchmark/xor/kernel.cu)                                   */
 /* ------------------------------------------------------------------------- */
