@@ -45,22 +45,32 @@ class HostPipeline:
         self.ev_done = [torch.cuda.Event() for _ in range(self.slots)]
         self.ev_free = [torch.cuda.Event() for _ in range(self.slots)]
         self.launches = 0
+        self._next = 0          # staging slots are used round-robin across calls
+        self._used = [False] * self.slots
+        self._joined = True     # the last call ended by joining the current stream
 
     def _range(self, c: int):
         lo = c * self.chunk
         return lo, min(lo + self.chunk, self.parity_bytes), min(lo + self.chunk, self.data_bytes)
 
-    def _run(self, inputs, outputs, work):
-        """inputs/outputs: lists of (shard index, host tensor); work(slot, nbytes_data, pbytes)."""
+    def _run(self, inputs, outputs, work, join: bool):
+        """inputs/outputs: lists of (shard index, host tensor); work(slot, nbytes_data, pbytes).
+
+        After a call with join=False the next call is not ordered after it on
+        the current stream: its copies in start as soon as staging slots free
+        up, overlapping the previous call's last kernels and copies out."""
         cur = torch.cuda.current_stream(self.device)
-        for s in (self.s_h2d, self.s_comp, self.s_d2h):
-            s.wait_stream(cur)
+        if self._joined:
+            for s in (self.s_h2d, self.s_comp, self.s_d2h):
+                s.wait_stream(cur)
         for c in range(self.nchunks):
-            sl = c % self.slots
+            sl = self._next % self.slots
+            self._next += 1
             lo, hi_p, hi_d = self._range(c)
             with torch.cuda.stream(self.s_h2d):
-                if c >= self.slots:
+                if self._used[sl]:
                     self.s_h2d.wait_event(self.ev_free[sl])
+                self._used[sl] = True
                 for idx, h in inputs:
                     hi = hi_d if idx < self.spec.k else hi_p
                     if hi > lo:
@@ -77,11 +87,21 @@ class HostPipeline:
                     if hi > lo:
                         h[lo:hi].copy_(self.buf[sl][idx][:hi - lo], non_blocking=True)
                 self.ev_free[sl].record(self.s_d2h)
-        cur.wait_stream(self.s_d2h)
+        self._joined = join
+        if join:
+            cur.wait_stream(self.s_d2h)
 
-    def encode(self, host_data: Sequence[torch.Tensor], host_parity: Sequence[torch.Tensor]) -> None:
-        """Enqueue the encode of pinned host shards; ordered before later work
-        on the current stream. Parity lands in host_parity."""
+    def join(self) -> None:
+        """Order the current stream after every call made so far."""
+        torch.cuda.current_stream(self.device).wait_stream(self.s_d2h)
+        self._joined = True
+
+    def encode(self, host_data: Sequence[torch.Tensor], host_parity: Sequence[torch.Tensor],
+               join: bool = True) -> None:
+        """Enqueue the encode of pinned host shards. Parity lands in host_parity;
+        with join (the default) it is ordered before later work on the current
+        stream, otherwise after the next join() (or joining call). Host inputs
+        must be ready when the call is made."""
         k = self.spec.k
 
         def work(sl, nd, np_):
@@ -93,11 +113,11 @@ class HostPipeline:
             self.launches += 1
 
         self._run([(i, host_data[i]) for i in range(k)],
-                  [(k + j, host_parity[j]) for j in range(self.spec.m)], work)
+                  [(k + j, host_parity[j]) for j in range(self.spec.m)], work, join)
 
-    def decode(self, host_shards: List[torch.Tensor], erased: Sequence[int]) -> None:
+    def decode(self, host_shards: List[torch.Tensor], erased: Sequence[int], join: bool = True) -> None:
         """Enqueue the rebuild of ``erased`` host shards (in place) from the
-        surviving host shards."""
+        surviving host shards (join as for encode)."""
         erased = list(erased)
         k = self.spec.k
         alive = [i for i in range(self.spec.n) if i not in erased]
@@ -107,4 +127,4 @@ class HostPipeline:
             codec.decode_ptrs(self.spec, ptrs, None, nd, nd, erased, 0, np_, int(self.s_comp.cuda_stream))
             self.launches += 1
 
-        self._run([(i, host_shards[i]) for i in alive], [(e, host_shards[e]) for e in erased], work)
+        self._run([(i, host_shards[i]) for i in alive], [(e, host_shards[e]) for e in erased], work, join)
