@@ -30,7 +30,6 @@ import functools
 import json
 import os
 import time
-from collections import OrderedDict, deque
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -38,6 +37,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, codec, ext
+from .store import ParityStore
 
 ENV_FLAG = "SGLANG_GATHER_KV_TO_GPU0"
 LOG_PREFIX = "[ft-rdp]"
@@ -79,10 +79,9 @@ class KVFaultTolerance:
         self._staging = None      # fused mode: registered KV staging (2 slots)
         self._peers = None
         self._parity = None
-        self._host_block = None   # pinned ring of parity slices (see _host_alloc)
-        self._host_gen = 0
-        self._host_head = 0
-        self._store = OrderedDict()  # chunk id -> parity slice record (oldest first)
+        # chunk id -> this rank's parity slice in pinned host memory
+        self._store = ParityStore(self.cfg.host_keep, self.cfg.host_budget, pin=True,
+                                  before_release=self._copies_landed)
         self._pending = []        # (record, event, t_enqueue) awaiting D2H completion
         self._copy_stream = None
         self._parity_free = [None, None]
@@ -91,7 +90,6 @@ class KVFaultTolerance:
         self._plans = {}          # (slot, half, stream) -> marshalled encode of that staging slot
         self._pools = {}          # KV pool geometry by (pointer, shape, strides)
         self._events = []         # timing events free for reuse
-        self._ring = deque()      # entries of the current pinned block in ring order
 
     # ------------------------------------------------------------- control --
     def _rank_world(self):
@@ -413,37 +411,11 @@ class KVFaultTolerance:
         self._drain(block=False)
         return plan["views"], (lo, hi)
 
-    def _host_alloc(self, nbytes: int):
-        """Pinned host bytes for one chunk's parity slice.
-
-        The store is a ring over one pinned block (pinning is slow, so it is
-        allocated once and only replaced by a larger one when a chunk does not
-        fit): chunks take consecutive byte ranges, wrapping at the end, and the
-        chunks whose bytes a new one overwrites are dropped (they are the oldest
-        in the block). At most host_keep chunks are kept. Chunks stored in a
-        replaced block stay readable until they are dropped by count."""
-        if self._host_block is None or nbytes > self._host_block.numel():
-            if self._copy_stream is not None:
-                # the block's bytes are written by raw copies the allocator does not
-                # track: let them land before the block can be released
-                self._copy_stream.synchronize()
-            size = max(4 * nbytes, min(self.cfg.host_budget, self.cfg.host_keep * nbytes))
-            self._host_block = torch.empty(size, dtype=torch.uint8, pin_memory=True)
-            self._host_gen += 1
-            self._host_head = 0
-            self._ring.clear()
-        if self._host_head + nbytes > self._host_block.numel():
-            self._host_head = 0
-        lo, hi = self._host_head, self._host_head + nbytes
-        # this block's entries sit in ring order: the ones the new bytes overwrite are at the front
-        while self._ring and self._ring[0]["off"] < hi and lo < self._ring[0]["off"] + self._ring[0]["size"]:
-            old = self._ring.popleft()
-            if self._store.get(old["cid"]) is old:
-                del self._store[old["cid"]]
-        while len(self._store) >= max(1, self.cfg.host_keep):
-            self._store.popitem(last=False)
-        self._host_head = hi
-        return self._host_block[lo:hi], dict(gen=self._host_gen, off=lo, size=nbytes)
+    def _copies_landed(self):
+        """The store's block is written by raw copies the allocator does not
+        track: let them land before the block can be released."""
+        if self._copy_stream is not None:
+            self._copy_stream.synchronize()
 
     def _offload(self, rec, parity, e0, e1, entry):
         """Copy this rank's parity slice to its pinned host slot on a side stream;
@@ -452,11 +424,8 @@ class KVFaultTolerance:
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(dev)
         nbytes = sum(t.numel() for t in parity)
-        old = self._store.pop(rec["chunk_id"], None)
-        if old is not None and old["gen"] == self._host_gen and old["size"] == nbytes:
-            host, place = old["host"], dict(gen=old["gen"], off=old["off"], size=nbytes)  # encoded again: same bytes
-        else:
-            host, place = self._host_alloc(nbytes)
+        stored = self._store.put(rec["chunk_id"], nbytes)
+        host = stored["host"]
         cs = self._copy_stream
         ready = self._event()
         ready.record(torch.cuda.current_stream(dev))
@@ -470,12 +439,7 @@ class KVFaultTolerance:
             _lib.check(copy(dst, t.data_ptr(), t.numel(), cs.cuda_stream))
             dst += t.numel()
         d1.record(cs)
-        entry.update(place, host=host, copied=d1, cid=rec["chunk_id"])
-        if old is None or entry["off"] != old["off"] or entry["gen"] != old["gen"]:
-            self._ring.append(entry)
-        else:  # same bytes as before: the ring keeps the earlier entry's place
-            self._ring = deque(entry if e is old else e for e in self._ring)
-        self._store[rec["chunk_id"]] = entry
+        stored.update(entry, copied=d1)
         self._pending.append((rec, (d0, d1), e0, e1))
         return d1
 
