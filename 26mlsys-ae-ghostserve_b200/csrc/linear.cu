@@ -74,13 +74,19 @@ __device__ void linear_tail(const LinearPass& a, int64_t t0) {
 // XORed by 64 consumer threads (16 bytes each), which store every output.
 constexpr int kLSeg = 1024;
 constexpr int kLLanes = kLSeg / 16;
-constexpr int kLStages = 3;
+constexpr int kLStages = 3;          // at least; narrow passes get more (see ring_stages)
+constexpr int kLRingBytes = 18 * 1024;  // bytes in flight per CTA the ring aims for
 static __device__ unsigned g_linear_status;
 
+// SPS 1 KiB segments of every input per stage: passes with few inputs take
+// several segments at once so the fixed cost of a stage (barrier wait and
+// release) is spread over more bytes.
+template <int SPS>
 __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass a, int nst) {
+  constexpr int ITEM = SPS * kLSeg;  // bytes of each input per stage
   extern __shared__ __align__(128) unsigned char smem[];
   const int nin = a.nin;
-  const int stage_bytes = nin * kLSeg;
+  const int stage_bytes = nin * ITEM;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)nst * stage_bytes);
   uint64_t* empty = full + nst;
   if (threadIdx.x == 0) {
@@ -92,7 +98,7 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
   }
   __syncthreads();
   const int64_t vend = a.begin + (((a.end - a.begin) >> 4) << 4);  // end of the whole-vector part
-  const int64_t items = (vend - a.begin + kLSeg - 1) / kLSeg;
+  const int64_t items = (vend - a.begin + ITEM - 1) / ITEM;
 
   if (threadIdx.x >= kLLanes) {  // producer warp: lane i copies input i of each stage
     const int pl = threadIdx.x - kLLanes;
@@ -109,12 +115,12 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
         }
         return;
       }
-      const int64_t off = a.begin + it * kLSeg;
-      const int64_t bytes = vend - off < kLSeg ? vend - off : kLSeg;
+      const int64_t off = a.begin + it * ITEM;
+      const int64_t bytes = vend - off < ITEM ? vend - off : ITEM;
       if (pl == 0) pipe::bar_expect_tx(full + r.stage, (uint32_t)(bytes * nin));
       __syncwarp();
       if (mine)
-        pipe::bulk_load_split(smem + (size_t)r.stage * stage_bytes + pl * kLSeg, my_lo, my_hi, a.split, off,
+        pipe::bulk_load_split(smem + (size_t)r.stage * stage_bytes + pl * ITEM, my_lo, my_hi, a.split, off,
                               (uint32_t)bytes, full + r.stage);
       r.next(nst);
       ++filled;
@@ -129,18 +135,45 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
       atomicOr(&g_linear_status, 2u);
       return;
     }
-    const int64_t off = a.begin + it * kLSeg + lane * 16;
+    const int64_t off0 = a.begin + it * ITEM + lane * 16;
     const uint4* st = reinterpret_cast<const uint4*>(smem + (size_t)r.stage * stage_bytes) + lane;
-    uint4 acc = vzero();
-    if (off < vend)
-      for (int i = 0; i < nin; ++i) acc = vxor(acc, st[i * kLLanes]);
+    uint4 acc[SPS];
+#pragma unroll
+    for (int q = 0; q < SPS; ++q) {
+      acc[q] = vzero();
+      if (off0 + q * kLSeg < vend)
+        for (int i = 0; i < nin; ++i) acc[q] = vxor(acc[q], st[i * SPS * kLLanes + q * kLLanes]);
+    }
     pipe::warp_release(empty + r.stage);
     r.next(nst);
-    if (off < vend)
-      for (int o = 0; o < a.nout; ++o)
-        if (off + 16 <= a.out_end[o]) st16(seg(a.out_lo[o], a.out_hi[o], a.split, off), acc);
+#pragma unroll
+    for (int q = 0; q < SPS; ++q) {
+      const int64_t off = off0 + q * kLSeg;
+      if (off < vend)
+        for (int o = 0; o < a.nout; ++o)
+          if (off + 16 <= a.out_end[o]) st16(seg(a.out_lo[o], a.out_hi[o], a.split, off), acc[q]);
+    }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, vend);
+}
+
+template <int SPS>
+int launch_xor(const LinearPass& a, cudaStream_t s) {
+  // keep ~18 KiB of loads in flight per CTA whatever the input count
+  int nst = kLRingBytes / (a.nin * SPS * kLSeg);
+  nst = nst < kLStages ? kLStages : (nst > 18 ? 18 : nst);
+  LaunchCache& cache = launch_cache();
+  auto k = xor_tma_kernel<SPS>;
+  const size_t smem = (size_t)nst * a.nin * SPS * kLSeg + 2 * (size_t)nst * sizeof(uint64_t);
+  int per_sm = cache.blocks_per_sm(k, kLLanes + 32, smem);
+  if (per_sm < 0) return check_launch("xor_tma launch shape");
+  per_sm = per_sm > 5 ? 5 : per_sm;
+  const int64_t items = ((a.end - a.begin) / 16 * 16 + SPS * kLSeg - 1) / (SPS * kLSeg);
+  int64_t grid = (int64_t)sm_count() * per_sm;
+  if (grid > items) grid = items;
+  if (grid < 1) grid = 1;
+  k<<<(int)grid, kLLanes + 32, smem, s>>>(a, nst);
+  return check_launch("xor_tma_kernel");
 }
 
 // ------------------------------------------------- GF(2^8), fixed input count
@@ -469,19 +502,8 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
     return check_launch("linear_scalar_kernel");
   }
   switch (a.field) {
-    case Field::XOR: {
-      LaunchCache& cache = launch_cache();
-      const size_t smem = (size_t)kLStages * a.nin * kLSeg + 2 * kLStages * sizeof(uint64_t);
-      int per_sm = cache.blocks_per_sm(xor_tma_kernel, kLLanes + 32, smem);
-      if (per_sm < 0) return check_launch("xor_tma launch shape");
-      per_sm = per_sm > 5 ? 5 : per_sm;
-      const int64_t items = ((a.end - a.begin) / 16 * 16 + kLSeg - 1) / kLSeg;
-      int64_t grid = (int64_t)sm_count() * per_sm;
-      if (grid > items) grid = items;
-      if (grid < 1) grid = 1;
-      xor_tma_kernel<<<(int)grid, kLLanes + 32, smem, s>>>(a, kLStages);
-      return check_launch("xor_tma_kernel");
-    }
+    case Field::XOR:
+      return a.nin <= 1 ? launch_xor<4>(a, s) : (a.nin <= 3 ? launch_xor<2>(a, s) : launch_xor<1>(a, s));
     case Field::GF8: {
       switch (a.nin) {
         case 1: return launch_gf8_fixed<1>(a, s);

@@ -414,14 +414,17 @@ int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
   if (a.unit % kSeg == 0) {  // TMA ring: units split into whole 1 KiB segments
     LaunchCache& cache = launch_cache();
     auto k = rdp_encode_tma_kernel<P>;
-    const size_t smem = (size_t)kStages * a.k * kSeg + 2 * kStages * sizeof(uint64_t);
+    // small k makes small stages: keep ~18 KiB of loads in flight per CTA all the same
+    int nst = 18 / a.k;
+    nst = nst < kStages ? kStages : (nst > 9 ? 9 : nst);
+    const size_t smem = (size_t)nst * a.k * kSeg + 2 * (size_t)nst * sizeof(uint64_t);
     int per_sm = cache.blocks_per_sm(k, kSegLanes + 32, smem);
     if (per_sm < 0) return check_launch("rdp_encode_tma launch shape");
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
     int64_t grid = (int64_t)sm_count() * per_sm;
     if (grid > items) grid = items;
-    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, kStages);
+    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, nst);
     return check_launch("rdp_encode_tma_kernel");
   }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
@@ -435,15 +438,18 @@ int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
   if (a.unit % kSeg == 0) {
     LaunchCache& cache = launch_cache();
     auto k = rdp_decode_tma_kernel<P>;
-    const size_t smem = (size_t)kDecStages * __builtin_popcount(a.alive) * kSeg + (size_t)2 * 2 * (P - 1) * kSeg +
-                        (2 * kDecStages + 4) * sizeof(uint64_t);
+    const int nalive = __builtin_popcount(a.alive);
+    int nst = 24 / nalive;  // ~24 KiB of loads in flight per CTA
+    nst = nst < kDecStages ? kDecStages : (nst > 12 ? 12 : nst);
+    const size_t smem = (size_t)nst * nalive * kSeg + (size_t)2 * 2 * (P - 1) * kSeg +
+                        (2 * (size_t)nst + 4) * sizeof(uint64_t);
     int per_sm = cache.blocks_per_sm(k, kDecThreads, smem);
     if (per_sm < 0) return check_launch("rdp_decode_tma launch shape");
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
     int64_t grid = (int64_t)sm_count() * per_sm;
     if (grid > items) grid = items;
-    k<<<(int)grid, kDecThreads, smem, s>>>(a, kDecStages);
+    k<<<(int)grid, kDecThreads, smem, s>>>(a, nst);
     return check_launch("rdp_decode_tma_kernel");
   }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);

@@ -228,7 +228,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill", "hook"])
+    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill", "hook", "sweep"])
+    ap.add_argument("--sweep-tokens", default="256,2048,8192", help="sweep workload: chunk sizes in tokens")
     ap.add_argument("--hook-tokens", type=int, default=2048, help="hook workload: tokens per extend call")
     ap.add_argument("--hook-modes", default="fused,reference", help="hook workload: modes to time")
     ap.add_argument("--prefill-seqs", type=int, default=16)
@@ -250,6 +251,9 @@ def main():
         return
     if args.workload == "hook":
         run_hook_bench(args)
+        return
+    if args.workload == "sweep":
+        run_sweep(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -354,7 +358,7 @@ def main():
                 "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
                 "kernel": ({"rdp": "rdp_encode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
                            if args.op == "encode" else
-                           {"rdp": "rdp_decode_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
+                           {"rdp": "rdp_decode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
                            )[wl["scheme"]]}
     if world > 1:
         link = 770.0
@@ -521,6 +525,143 @@ def run_hook_bench(args):
         }
         if "fused" in out and "reference" in out:
             line["speedup_vs_reference_flow"] = round(out["reference"]["us_per_call"] / out["fused"]["us_per_call"], 2)
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+SWEEP_CODES = ([("xor", k, 1, 0) for k in range(1, 8)] + [("rdp", p - 1, 2, p) for p in (3, 5, 7)] +
+               [("rs8", k, 2, 0) for k in range(2, 7)])
+
+
+def run_sweep(args):
+    """Config 4: encode and worst-case decode (data shards 0..m-1 lost) GB/s
+    (device time of back-to-back launches replayed from a CUDA graph)
+    for XOR k=1..7, textbook RDP p=3/5/7 (k = p-1), RS(k,2) k=2..6, at chunk
+    sizes of 256/2048/8192 tokens of bf16 or fp8 KV (32 layers x 1 KV head x
+    128 per rank: 16 KiB of K+V per bf16 token), random bytes. At N GPUs each
+    rank encodes its own codeword whose shard j sits on GPU (rank+j) % N (the
+    bench's placement), so remote shards are read over NVLink. Rank 0 adds the
+    CPU port's rate on a 16 MiB-per-shard sample of each code."""
+    import importlib
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, device = init_nccl()
+    g = importlib.import_module(PKG)
+    p2p = importlib.import_module(PKG + ".p2p")
+    peak, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream()
+    cap = torch.cuda.Stream()  # the codec calls are bound to this stream and captured in CUDA graphs
+    sh = int(cap.cuda_stream)
+    tokens_list = [int(t) for t in args.sweep_tokens.split(",")]
+    rows = []
+    cpu_rates = {}
+    for scheme, k, m, p in SWEEP_CODES:
+        spec = g.CodeSpec(scheme, k, m, p, 4096 if scheme == "rdp" else 0)
+        for kv in ("bf16", "fp8"):
+            for tokens in tokens_list:
+                nbytes = tokens * 32 * 128 * 2 * (2 if kv == "bf16" else 1)
+                pbytes = spec.parity_bytes(nbytes)
+                gen = torch.Generator(device=device).manual_seed(1000 * rank + tokens + k)
+                slots = [torch.randint(0, 256, (nbytes,), generator=gen, device=device, dtype=torch.uint8)
+                         for _ in range(k)]
+                parity = [torch.empty(pbytes, dtype=torch.uint8, device=device) for _ in range(m)]
+                group = None
+                if world > 1:
+                    group = p2p.PeerGroup.create(slots)
+                    data = [group.ptr((rank + j) % world, j) for j in range(k)]
+                    remote = sum(nbytes for j in range(k) if (rank + j) % world != rank)
+                else:
+                    data, remote = [t.data_ptr() for t in slots], 0
+                enc = g.codec.PreparedEncode(spec, data, None, nbytes, nbytes, [t.data_ptr() for t in parity],
+                                             0, pbytes, sh)
+                erased = list(range(min(m, k)))
+                rebuilt = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in erased]
+                ptrs = list(data) + [t.data_ptr() for t in parity]
+                for e, t in zip(erased, rebuilt):
+                    ptrs[e] = t.data_ptr()
+                dec = g.codec.PreparedDecode(spec, ptrs, None, nbytes, nbytes, erased, 0, pbytes, sh)
+                enc_bytes = k * nbytes + m * pbytes
+                dec_bytes = k * nbytes + len(erased) * nbytes  # survivors read (k of them) + rebuilt written
+
+                def timed(fn, est_bytes):
+                    # reps launches captured in one CUDA graph: device time, not host launch rate
+                    reps = max(5, min(200, int(0.02 / (est_bytes / 5e12))))
+                    cap.wait_stream(stream)
+                    for _ in range(3):
+                        fn()
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=cap):
+                        for _ in range(reps):
+                            fn()
+                    torch.cuda.synchronize()
+                    graph.replay()  # warm
+                    torch.cuda.synchronize()
+                    if world > 1:
+                        dist.barrier()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    graph.replay()
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    del graph
+                    t = torch.tensor([e0.elapsed_time(e1) / reps], device=device, dtype=torch.float64)
+                    if world > 1:
+                        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    return float(t.item())
+
+                if world > 1:
+                    dist.barrier()
+                ms_e = timed(enc, enc_bytes)
+                ms_d = timed(dec, dec_bytes)
+                ok = all(torch.equal(t, slots[e]) for e, t in zip(erased, rebuilt)) if world == 1 else None
+                if world > 1:  # the rebuilt shards are copies of (possibly remote) shards: compare there
+                    flags = torch.tensor([0], device=device)
+                    for e, t in zip(erased, rebuilt):
+                        src = torch.empty(nbytes, dtype=torch.uint8, device=device)
+                        g._lib.call("gsec_copy_async", g._lib.C.c_void_p(src.data_ptr()), g._lib.C.c_void_p(data[e]),
+                                    nbytes, g._lib.C.c_void_p(sh))
+                        flags += 0 if torch.equal(src, t) else 1
+                    dist.all_reduce(flags)
+                    ok = int(flags.item()) == 0
+                row = {"code": scheme, "k": k, "m": m, "p": p, "kv": kv, "tokens": tokens, "shard_bytes": nbytes,
+                       "enc_gbs": round(enc_bytes / (ms_e * 1e-3) / 1e9, 1),
+                       "enc_frac": round(enc_bytes / (ms_e * 1e-3) / 1e9 / peak, 3),
+                       "dec_gbs": round(dec_bytes / (ms_d * 1e-3) / 1e9, 1),
+                       "dec_frac": round(dec_bytes / (ms_d * 1e-3) / 1e9 / peak, 3),
+                       "erased": erased, "verified": ok}
+                if world > 1:
+                    link = 770.0
+                    # the decode reads only the survivors: the lost shards' remote bytes do not cross NVLink
+                    dec_remote = sum(nbytes for j in range(k) if j not in erased and (rank + j) % world != rank)
+                    for key, ms, tot, rem in (("enc", ms_e, enc_bytes, remote), ("dec", ms_d, dec_bytes, dec_remote)):
+                        roof = max((tot - rem) / (peak * 1e9), rem / (link * 1e9))
+                        row[key + "_roof_frac"] = round(roof * 1e3 / ms, 3)
+                    row["remote_bytes"] = remote
+                rows.append(row)
+                if group is not None:
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    group.close()
+                del slots, parity, rebuilt
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            wl = dict(scheme=scheme, k=k, m=m, p=p, unit=4096 if scheme == "rdp" else 0, shard=16 * MIB, kv="u8")
+            rng = np.random.default_rng(k)
+            host = [rng.integers(0, 256, 16 * MIB, dtype=np.uint8) for _ in range(k)]
+            rate, reps, threads, el = cpu_encode_rate(wl, host, 0.5)
+            cpu_rates[f"{scheme}_k{k}_m{m}"] = {"gbs": round(rate, 2), "cores": threads}
+    if rank == 0:
+        fr = [r["enc_frac"] for r in rows]
+        line = {"metric": "KV parity encode/decode GB/s per GPU sweep (config 4)", "value": round(min(fr), 3),
+                "unit": "min encode fraction of measured HBM peak", "n_gpus": world, "higher_is_better": True,
+                "scaling": "weak", "dtype": "u8", "data": "synthetic (uniform random bytes)",
+                "peak": peak, "peak_kind": peak_kind,
+                "config": {"workload": "sweep", "tokens": tokens_list,
+                           "shard": "tokens x 32 layers x 1 kv head x 128 x (K,V) x (2 B bf16 | 1 B fp8)"},
+                "rows": rows, "cpu_port": cpu_rates or None}
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
