@@ -96,6 +96,42 @@ __device__ __forceinline__ uint4 vxor(uint4 a, uint4 b) {
 
 __device__ __forceinline__ uint4 vzero() { return make_uint4(0u, 0u, 0u, 0u); }
 
+// 16 bytes starting at any byte address p, assembled from the aligned 16-byte
+// block(s) that hold them: one block when p is aligned, else two, both of which
+// contain bytes of [p, p + 16) (so nothing outside the aligned span of the
+// requested bytes is read). Plain cached loads: a neighbouring thread reads the
+// same blocks.
+__device__ __forceinline__ uint4 ldu16(const void* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t m = (uint32_t)(a & 15u);
+  const uint4* q = reinterpret_cast<const uint4*>(a - m);
+  const uint4 lo = q[0];
+  if (m == 0) return lo;
+  const uint4 hi = q[1];
+  const uint32_t e[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  const uint32_t sh = (m & 3u) * 8u;
+  uint32_t o[4];
+  switch (m >> 2) {  // whole words of the shift; the byte part is a funnel shift
+    case 0:
+#pragma unroll
+      for (int l = 0; l < 4; ++l) o[l] = __funnelshift_r(e[l], e[l + 1], sh);
+      break;
+    case 1:
+#pragma unroll
+      for (int l = 0; l < 4; ++l) o[l] = __funnelshift_r(e[l + 1], e[l + 2], sh);
+      break;
+    case 2:
+#pragma unroll
+      for (int l = 0; l < 4; ++l) o[l] = __funnelshift_r(e[l + 2], e[l + 3], sh);
+      break;
+    default:
+#pragma unroll
+      for (int l = 0; l < 4; ++l) o[l] = __funnelshift_r(e[l + 3], e[l + 4], sh);
+      break;
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // ------------------------------------------------------------- GF(2^8) ------
 // Field GF(2)[x]/(x^8+x^4+x^3+x^2+1) (0x11d), generator x (= 2).
 

@@ -54,13 +54,37 @@ __global__ void rows_pack_vec(const char* s0, int64_t len0, const char* s1, int6
   }
 }
 
-__global__ void rows_pack_byte(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
-                               int64_t pitch, int64_t row_bytes, int nrows) {
-  const int64_t total = row_bytes * nrows;
+// Any alignment: every row is written with aligned 16-byte stores (its first
+// bytes up to the first aligned address, and its last partial vector, byte by
+// byte); the stream is read with ldu16 windows.
+__device__ __forceinline__ char stream_byte(const char* s0, int64_t len0, const char* s1, int64_t stream,
+                                            int64_t j) {
+  return j < len0 ? s0[j] : (j < stream ? s1[j - len0] : (char)0);
+}
+
+__global__ void rows_pack_any(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
+                              int64_t pitch, int64_t row_bytes, int nrows) {
+  const int64_t slots = (row_bytes >> 4) + 2;  // head + whole vectors + tail of a row
+  const int64_t total = slots * nrows;
   const int64_t stream = len0 + len1;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / row_bytes, x = i - r * row_bytes;
-    rows[r * pitch + x] = i < len0 ? s0[i] : (i < stream ? s1[i - len0] : (char)0);
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = g / slots, j = g - r * slots;
+    char* base = rows + r * pitch;
+    int64_t h = (16 - (int64_t)(reinterpret_cast<uintptr_t>(base) & 15u)) & 15;
+    if (h > row_bytes) h = row_bytes;
+    const int64_t x0 = j == 0 ? 0 : h + (j - 1) * 16;
+    const int64_t x1 = j == 0 ? h : (x0 + 16 < row_bytes ? x0 + 16 : row_bytes);
+    if (x0 >= x1) continue;
+    const int64_t i = r * row_bytes + x0;  // stream offset of base[x0]
+    if (x1 - x0 == 16 && i + 16 <= len0) {
+      stv(base + x0, ldu16(s0 + i));
+    } else if (x1 - x0 == 16 && i >= len0 && i + 16 <= stream) {
+      stv(base + x0, ldu16(s1 + (i - len0)));
+    } else if (x1 - x0 == 16 && i >= stream) {
+      stv(base + x0, vzero());
+    } else {
+      for (int64_t x = x0; x < x1; ++x) base[x] = stream_byte(s0, len0, s1, stream, r * row_bytes + x);
+    }
   }
 }
 
@@ -86,14 +110,32 @@ __global__ void rows_unpack_vec(const char* rows, int64_t pitch, int64_t row_byt
   }
 }
 
-__global__ void rows_unpack_byte(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
-                                 char* d1, int64_t len1) {
-  const int64_t stream = len0 + len1;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < stream; i += (int64_t)gridDim.x * blockDim.x) {
+// Any alignment: each destination (d0, then d1) is written with aligned
+// 16-byte stores, its unaligned head and last partial vector byte by byte; a
+// vector whose 16 source bytes lie in one row is read with an ldu16 window.
+__global__ void rows_unpack_any(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
+                                char* d1, int64_t len1) {
+  const int64_t na = (len0 >> 4) + 2, nb = (len1 >> 4) + 2;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < na + nb; g += (int64_t)gridDim.x * blockDim.x) {
+    const bool first = g < na;
+    char* dst = first ? d0 : d1;
+    const int64_t len = first ? len0 : len1, soff = first ? 0 : len0, j = first ? g : g - na;
+    if (len == 0) continue;
+    int64_t h = (16 - (int64_t)(reinterpret_cast<uintptr_t>(dst) & 15u)) & 15;
+    if (h > len) h = len;
+    const int64_t x0 = j == 0 ? 0 : h + (j - 1) * 16;
+    const int64_t x1 = j == 0 ? h : (x0 + 16 < len ? x0 + 16 : len);
+    if (x0 >= x1) continue;
+    const int64_t i = soff + x0;  // stream offset of dst[x0]
     const int64_t r = i / row_bytes, x = i - r * row_bytes;
-    const char c = rows[r * pitch + x];
-    if (i < len0) d0[i] = c;
-    else d1[i - len0] = c;
+    if (x1 - x0 == 16 && x + 16 <= row_bytes) {
+      stv(dst + x0, ldu16(rows + r * pitch + x));
+    } else {
+      for (int64_t b = x0; b < x1; ++b) {
+        const int64_t ii = soff + b, rr = ii / row_bytes;
+        dst[b] = rows[rr * pitch + (ii - rr * row_bytes)];
+      }
+    }
   }
 }
 
@@ -154,6 +196,77 @@ __global__ void bhtd_unpack_kernel(const uint16_t* rows, int64_t pitch, int64_t 
   }
 }
 
+// Any alignment (D, S, pitch or a tensor not multiples of 8 words / 16 bytes):
+// rows are written with aligned 16-byte stores (unaligned head and last partial
+// vector word by word); 8 stream words that are 8 consecutive source words
+// (same token, same [b,h], d + 8 <= D) are read with one ldu16 window.
+__device__ __forceinline__ uint16_t bhtd_word(const uint16_t* k, const uint16_t* v, const Perm& p, int64_t i) {
+  return i < p.Tn ? k[perm_src(p, i)] : (i < 2 * p.Tn ? v[perm_src(p, i - p.Tn)] : (uint16_t)0);
+}
+
+__global__ void bhtd_pack_any(const uint16_t* k, const uint16_t* v, Perm p, uint16_t* rows, int64_t pitch,
+                              int64_t S, int nd) {
+  const int64_t slots = (S >> 3) + 2;
+  const int64_t total = slots * nd;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = g / slots, j = g - r * slots;
+    uint16_t* base = rows + r * pitch;
+    int64_t h = ((16 - (int64_t)(reinterpret_cast<uintptr_t>(base) & 15u)) & 15) >> 1;  // words
+    if (h > S) h = S;
+    const int64_t c0 = j == 0 ? 0 : h + (j - 1) * 8;
+    const int64_t c1 = j == 0 ? h : (c0 + 8 < S ? c0 + 8 : S);
+    if (c0 >= c1) continue;
+    const int64_t i0 = r * S + c0;
+    bool done = false;
+    if (c1 - c0 == 8 && (reinterpret_cast<uintptr_t>(base + c0) & 15u) == 0) {
+      if (i0 >= 2 * p.Tn) {
+        stv(base + c0, vzero());
+        done = true;
+      } else if (i0 + 8 <= p.Tn || (i0 >= p.Tn && i0 + 8 <= 2 * p.Tn)) {
+        const int64_t jj = i0 < p.Tn ? i0 : i0 - p.Tn;
+        const int64_t t = jj / p.n, c = jj - t * p.n, d = c % p.D;
+        if (d + 8 <= p.D) {
+          stv(base + c0, ldu16((i0 < p.Tn ? k : v) + perm_src(p, jj)));
+          done = true;
+        }
+      }
+    }
+    if (!done)
+      for (int64_t c = c0; c < c1; ++c) base[c] = bhtd_word(k, v, p, r * S + c);
+  }
+}
+
+// Inverse: the K and V tensors are written in [B,H,T,D] order with aligned
+// 16-byte stores; 8 destination words in one [b,h,t] run of D come from 8
+// consecutive stream words, read with one ldu16 window when they lie in one row.
+__global__ void bhtd_unpack_any(const uint16_t* rows, int64_t pitch, int64_t S, Perm p, uint16_t* k,
+                                uint16_t* v) {
+  const int64_t per = (p.Tn >> 3) + 2;  // slots of one tensor
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < 2 * per; g += (int64_t)gridDim.x * blockDim.x) {
+    const bool isk = g < per;
+    uint16_t* dst = isk ? k : v;
+    const int64_t j = isk ? g : g - per, toff = isk ? 0 : p.Tn;
+    int64_t h = ((16 - (int64_t)(reinterpret_cast<uintptr_t>(dst) & 15u)) & 15) >> 1;
+    if (h > p.Tn) h = p.Tn;
+    const int64_t w0 = j == 0 ? 0 : h + (j - 1) * 8;
+    const int64_t w1 = j == 0 ? h : (w0 + 8 < p.Tn ? w0 + 8 : p.Tn);
+    if (w0 >= w1) continue;
+    // destination word w = ((bh * T + t) * D + d)  ->  stream word t * n + bh * D + d
+    const int64_t d = w0 % p.D, bt = w0 / p.D, t = bt % p.T, bh = bt / p.T;
+    const int64_t i = toff + t * p.n + bh * p.D + d;
+    const int64_t r = i / S, x = i - r * S;
+    if (w1 - w0 == 8 && d + 8 <= p.D && x + 8 <= S && (reinterpret_cast<uintptr_t>(dst + w0) & 15u) == 0) {
+      stv(dst + w0, ldu16(rows + r * pitch + x));
+    } else {
+      for (int64_t w = w0; w < w1; ++w) {
+        const int64_t dd = w % p.D, b2 = w / p.D, tt = b2 % p.T, bb = b2 / p.T;
+        const int64_t ii = toff + tt * p.n + bb * p.D + dd, rr = ii / S;
+        dst[w] = rows[rr * pitch + (ii - rr * S)];
+      }
+    }
+  }
+}
+
 }  // namespace
 
 int rows_pack(const void* s0, int64_t len0, const void* s1, int64_t len1, void* rows, int64_t pitch,
@@ -171,7 +284,7 @@ int rows_pack(const void* s0, int64_t len0, const void* s1, int64_t len1, void* 
     rows_pack_vec<<<grid_cap((row_bytes >> 4) * nrows, threads), threads, 0, s>>>(
         a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
   } else {
-    rows_pack_byte<<<grid_cap(row_bytes * nrows, threads), threads, 0, s>>>(
+    rows_pack_any<<<grid_cap(((row_bytes >> 4) + 2) * nrows, threads), threads, 0, s>>>(
         a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
   }
   return check_launch("rows_pack");
@@ -192,7 +305,7 @@ int rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int nrows, v
     rows_unpack_vec<<<grid_cap((len0 + len1 + 15) >> 4, threads), threads, 0, s>>>(
         static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
   } else {
-    rows_unpack_byte<<<grid_cap(len0 + len1, threads), threads, 0, s>>>(
+    rows_unpack_any<<<grid_cap((len0 >> 4) + (len1 >> 4) + 4, threads), threads, 0, s>>>(
         static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
   }
   return check_launch("rows_unpack");
@@ -205,6 +318,10 @@ int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_
   GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_pack: rows too small");
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
+  if (!vec) {
+    bhtd_pack_any<<<grid_cap(((S >> 3) + 2) * nd, threads), threads, 0, s>>>(k, v, p, rows, pitch, S, nd);
+    return check_launch("bhtd_pack_any");
+  }
   bhtd_pack_kernel<<<grid_cap(((S + 7) >> 3) * nd, threads), threads, 0, s>>>(k, v, p, rows, pitch, S, nd, vec);
   return check_launch("bhtd_pack_kernel");
 }
@@ -216,6 +333,10 @@ int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t
   GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_unpack: rows too small");
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
+  if (!vec) {
+    bhtd_unpack_any<<<grid_cap(2 * ((p.Tn >> 3) + 2), threads), threads, 0, s>>>(rows, pitch, S, p, k, v);
+    return check_launch("bhtd_unpack_any");
+  }
   bhtd_unpack_kernel<<<grid_cap((2 * p.Tn + 7) >> 3, threads), threads, 0, s>>>(rows, pitch, S, p, k, v, vec);
   return check_launch("bhtd_unpack_kernel");
 }

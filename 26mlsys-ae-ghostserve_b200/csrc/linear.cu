@@ -40,10 +40,11 @@ __device__ __forceinline__ void st16(char* p, uint4 v) {
                : "memory");
 }
 
-// Sub-vector tail [t0, end) of every output, one thread, symbol at a time.
-__device__ void linear_tail(const LinearPass& a, int64_t t0) {
+// Bytes [t0, t1) of every output (a pass's unaligned head or sub-vector tail),
+// one thread, symbol at a time.
+__device__ void linear_range(const LinearPass& a, int64_t t0, int64_t t1) {
   if (a.field == Field::GF16) {
-    for (int64_t x = t0; x + 2 <= a.end; x += 2) {
+    for (int64_t x = t0; x + 2 <= t1; x += 2) {
       for (int j = 0; j < a.nout; ++j) {
         uint32_t acc = 0;
         for (int i = 0; i < a.nin; ++i) {
@@ -56,7 +57,7 @@ __device__ void linear_tail(const LinearPass& a, int64_t t0) {
     }
     return;
   }
-  for (int64_t x = t0; x < a.end; ++x) {
+  for (int64_t x = t0; x < t1; ++x) {
     for (int j = 0; j < a.nout; ++j) {
       uint32_t acc = 0;
       for (int i = 0; i < a.nin; ++i) {
@@ -66,6 +67,11 @@ __device__ void linear_tail(const LinearPass& a, int64_t t0) {
       if (x < a.out_end[j]) *reinterpret_cast<uint8_t*>(seg(a.out_lo[j], a.out_hi[j], a.split, x)) = (uint8_t)acc;
     }
   }
+}
+
+__device__ __forceinline__ void linear_tail(const LinearPass& a, int64_t t0) {
+  linear_range(a, t0, a.end);
+  if (a.head > 0) linear_range(a, a.begin - a.head, a.begin);
 }
 
 // ------------------------------------------------------- XOR (TMA ring) -----
@@ -322,7 +328,7 @@ __global__ void __launch_bounds__(1024) gf8_vec_kernel(const LinearPass a) {
 // -------------------------------------------------------------- GF(2^16) ----
 // Constant multiply c*w = c*(w & 0xff) ^ c*(w & 0xff00): two byte tables per
 // input, entries pack the u16 products of outputs 0 (low half) and 1 (high).
-template <int NOUT, int R>
+template <int NOUT, int R, bool U>
 __global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
   extern __shared__ uint32_t tab[];  // [nin][2][256][R]
   for (int e = threadIdx.x; e < a.nin * 512; e += blockDim.x) {
@@ -346,7 +352,7 @@ __global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
     for (int j = 0; j < NOUT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0u;
 #pragma unroll 2
     for (int i = 0; i < a.nin; ++i) {
-      const uint4 xv = ld16(seg(a.in_lo[i], a.in_hi[i], a.split, off));
+      const uint4 xv = U ? ldu16(a.in_lo[i] + off) : ld16(seg(a.in_lo[i], a.in_hi[i], a.split, off));
       const uint32_t* tlo = tl + (size_t)i * 512 * R;
       const uint32_t* thi = tlo + 256 * R;
       const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -363,6 +369,23 @@ __global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
     for (int j = 0; j < NOUT; ++j)
       if (off + 16 <= a.out_end[j])
         st16(seg(a.out_lo[j], a.out_hi[j], a.split, off), make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
+}
+
+// ------------------------------------------------- XOR, unaligned inputs ----
+// Inputs at any byte alignment (the bulk copies of the ring need 16-byte
+// aligned sources): each thread XORs ldu16 windows of every input into an
+// aligned 16-byte store of every output. Contiguous shards only.
+__global__ void __launch_bounds__(256) xor_unaligned_kernel(const LinearPass a) {
+  const int64_t nvec = (a.end - a.begin) >> 4;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
+    const int64_t off = a.begin + (v << 4);
+    uint4 acc = vzero();
+    for (int i = 0; i < a.nin; ++i) acc = vxor(acc, ldu16(a.in_lo[i] + off));
+    for (int o = 0; o < a.nout; ++o)
+      if (off + 16 <= a.out_end[o]) st16(a.out_lo[o] + off, acc);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
 }
@@ -430,10 +453,10 @@ int launch_gf8(const LinearPass& a, cudaStream_t s) {
   return check_launch("gf8_vec_kernel");
 }
 
-template <int NOUT, int R>
+template <int NOUT, int R, bool U>
 int launch_gf16(const LinearPass& a, cudaStream_t s) {
   const size_t smem = (size_t)a.nin * 512 * 4 * R;
-  auto k = gf16_vec_kernel<NOUT, R>;
+  auto k = gf16_vec_kernel<NOUT, R, U>;
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
   k<<<grid, threads, smem, s>>>(a);
@@ -462,15 +485,15 @@ int dispatch_gf8(const LinearPass& a, int r, cudaStream_t s) {
     default: return launch_gf8<NOUT, 1>(a, s);
   }
 }
-template <int NOUT>
+template <int NOUT, bool U>
 int dispatch_gf16(const LinearPass& a, int r, cudaStream_t s) {
   switch (r) {
-    case 32: return launch_gf16<NOUT, 32>(a, s);
-    case 16: return launch_gf16<NOUT, 16>(a, s);
-    case 8: return launch_gf16<NOUT, 8>(a, s);
-    case 4: return launch_gf16<NOUT, 4>(a, s);
-    case 2: return launch_gf16<NOUT, 2>(a, s);
-    default: return launch_gf16<NOUT, 1>(a, s);
+    case 32: return launch_gf16<NOUT, 32, U>(a, s);
+    case 16: return launch_gf16<NOUT, 16, U>(a, s);
+    case 8: return launch_gf16<NOUT, 8, U>(a, s);
+    case 4: return launch_gf16<NOUT, 4, U>(a, s);
+    case 2: return launch_gf16<NOUT, 2, U>(a, s);
+    default: return launch_gf16<NOUT, 1, U>(a, s);
   }
 }
 
@@ -488,19 +511,74 @@ unsigned linear_device_status(bool clear) {
   return v;
 }
 
+namespace {
+int run_scalar(const LinearPass& a, cudaStream_t s) {
+  const int threads = 256;
+  const int64_t nsym = (a.end - a.begin) / (a.field == Field::GF16 ? 2 : 1);
+  const int grid = occupancy_grid(linear_scalar_kernel, threads, 0, nsym);
+  linear_scalar_kernel<<<grid, threads, 0, s>>>(a);
+  return check_launch("linear_scalar_kernel");
+}
+
+// Layouts whose pointers are not 16-byte aligned (the reference's [rows, S]
+// tensors with S not a multiple of 16 bytes). XOR and GF(2^16) passes over
+// contiguous shards run with aligned stores and ldu16 input windows: outputs
+// are grouped by their address mod 16, and each group's pass starts at the
+// first offset where its outputs are aligned (the bytes before that go to the
+// scalar kernel). Anything else keeps the scalar kernel.
+int run_unaligned(const LinearPass& a, cudaStream_t s) {
+  const bool contiguous = a.split >= a.end;
+  const bool field_ok = a.field == Field::XOR || (a.field == Field::GF16 && (a.begin & 1) == 0);
+  if (!contiguous || !field_ok || (a.end - a.begin) < 256) return run_scalar(a, s);
+  bool done[kLinMaxOut] = {};
+  for (int j = 0; j < a.nout; ++j) {
+    if (done[j]) continue;
+    const uintptr_t cls = reinterpret_cast<uintptr_t>(a.out_lo[j]) & 15u;
+    LinearPass b = a;
+    b.nout = 0;
+    for (int q = j; q < a.nout; ++q) {
+      if (done[q] || (reinterpret_cast<uintptr_t>(a.out_lo[q]) & 15u) != cls) continue;
+      done[q] = true;
+      b.out_lo[b.nout] = a.out_lo[q];
+      b.out_hi[b.nout] = a.out_hi[q];
+      b.out_end[b.nout] = a.out_end[q];
+      for (int i = 0; i < a.nin; ++i) b.coef[b.nout][i] = a.coef[q][i];
+      ++b.nout;
+    }
+    int64_t x = a.begin;
+    while (((reinterpret_cast<uintptr_t>(b.out_lo[0]) + (uintptr_t)x) & 15u) && x < a.end) ++x;
+    if (a.field == Field::GF16 && ((x - a.begin) & 1)) return run_scalar(a, s);  // odd byte output base
+    if (x >= a.end) {
+      const int rc = run_scalar(b, s);
+      if (rc) return rc;
+      continue;
+    }
+    b.begin = x;
+    b.head = x - a.begin;  // done by the vector kernel's first thread with its tail
+    int rc;
+    if (a.field == Field::XOR) {
+      const int threads = 256;
+      const int grid = occupancy_grid(xor_unaligned_kernel, threads, 0, (b.end - b.begin) >> 4);
+      xor_unaligned_kernel<<<grid, threads, 0, s>>>(b);
+      rc = check_launch("xor_unaligned_kernel");
+    } else {
+      if (b.nout > 2) return run_scalar(a, s);
+      const int r = pick_replicas((int64_t)b.nin * 512 * 4, kTableBudget);
+      rc = b.nout == 1 ? dispatch_gf16<1, true>(b, r, s) : dispatch_gf16<2, true>(b, r, s);
+    }
+    if (rc) return rc;
+  }
+  return GSEC_OK;
+}
+}  // namespace
+
 int run_linear(const LinearPass& a, cudaStream_t s) {
   if (a.end <= a.begin || a.nout == 0) return GSEC_OK;
   if (a.nin < 1 || a.nin > kLinMaxIn || a.nout < 0 || a.nout > kLinMaxOut) {
     set_error("linear pass: nin=%d nout=%d out of range", a.nin, a.nout);
     return GSEC_EINVAL;
   }
-  if (!pass_aligned(a)) {
-    const int threads = 256;
-    const int64_t nsym = (a.end - a.begin) / (a.field == Field::GF16 ? 2 : 1);
-    const int grid = occupancy_grid(linear_scalar_kernel, threads, 0, nsym);
-    linear_scalar_kernel<<<grid, threads, 0, s>>>(a);
-    return check_launch("linear_scalar_kernel");
-  }
+  if (!pass_aligned(a)) return run_unaligned(a, s);
   switch (a.field) {
     case Field::XOR:
       return a.nin <= 1 ? launch_xor<4>(a, s) : (a.nin <= 3 ? launch_xor<2>(a, s) : launch_xor<1>(a, s));
@@ -530,7 +608,7 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
         return GSEC_EINVAL;
       }
       const int r = pick_replicas((int64_t)a.nin * 512 * 4, kTableBudget);
-      return a.nout == 1 ? dispatch_gf16<1>(a, r, s) : dispatch_gf16<2>(a, r, s);
+      return a.nout == 1 ? dispatch_gf16<1, false>(a, r, s) : dispatch_gf16<2, false>(a, r, s);
     }
   }
   return GSEC_EINVAL;

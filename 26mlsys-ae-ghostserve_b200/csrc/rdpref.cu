@@ -67,29 +67,37 @@ __device__ __forceinline__ uint4 clear_lane(uint4 v, int i) {
   return v;
 }
 
-__device__ __forceinline__ int64_t mod_s(int64_t x, int64_t S) {
-  int64_t r = x % S;
-  return r < 0 ? r + S : r;
+// (x mod S) for x > -nd: one add unless S < nd (tiny shards), then a modulo.
+__device__ __forceinline__ int64_t wrap_s(int64_t x, int64_t S) {
+  if (x >= 0) return x;
+  x += S;
+  return x >= 0 ? x : ((x % S) + S) % S;
 }
 
 // excl[r]: the Q position whose row-r term is skipped, or -1.
+// ND > 0: the row count as a compile-time constant, so every row's loads are
+// independent straight-line code (all in flight at once); ND = 0: any count.
+template <int ND>
 __global__ void __launch_bounds__(256) rdpref_parity_kernel(RdpRefParityArgs a) {
+  const int nd = ND > 0 ? ND : a.nd;
   const int64_t S = a.S;
   const int64_t nvec = (S + 7) >> 3;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
-  uint16_t* prow = a.rows + (int64_t)a.nd * a.pitch;
-  uint16_t* qrow = a.rows + (int64_t)(a.nd + 1) * a.pitch;
+  uint16_t* prow = a.rows + (int64_t)nd * a.pitch;
+  uint16_t* qrow = a.rows + (int64_t)(nd + 1) * a.pitch;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nvec; t += step) {
     const int64_t d0 = t << 3;
-    const bool interior = a.vec_ok && d0 >= (int64_t)(a.nd - 1) && d0 + 8 <= S;
+    const bool interior = a.vec_ok && d0 >= (int64_t)(nd - 1) && d0 + 8 <= S;
     if (interior) {
       uint4 p = vzero(), q = vzero();
-      for (int rb = 0; rb < a.nd; rb += 8) {
+#pragma unroll
+      for (int rb = 0; rb < (ND > 0 ? ND : kRefMaxNd); rb += 8) {
+        if (ND == 0 && rb >= nd) break;
         const int64_t vq = rb >> 3;  // whole-vector shift of this group of rows
 #pragma unroll
         for (int w = 0; w < 8; ++w) {  // word shift; a literal after unrolling
           const int r = rb + w;
-          if (r >= a.nd) break;
+          if (r >= nd) break;
           const uint16_t* row = a.rows + (int64_t)r * a.pitch;
           const uint4 at_d0 = ld16c(row + d0);
           p = vxor(p, at_d0);
@@ -104,19 +112,80 @@ __global__ void __launch_bounds__(256) rdpref_parity_kernel(RdpRefParityArgs a) 
       *reinterpret_cast<uint4*>(prow + d0) = p;
       *reinterpret_cast<uint4*>(qrow + d0) = q;
     } else {
+      // the wrapping head (d0 < nd - 1) and the partial tail: word by word, with
+      // every row's two loads independent of each other
       const int64_t dend = d0 + 8 < S ? d0 + 8 : S;
-      for (int64_t d = d0; d < dend; ++d) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int64_t d = d0 + e;
+        if (d >= dend) break;
         uint16_t pacc = 0, qacc = 0;
-        for (int r = 0; r < a.nd; ++r) {
+#pragma unroll
+        for (int r = 0; r < (ND > 0 ? ND : kRefMaxNd); ++r) {
+          if (ND == 0 && r >= nd) break;
           const uint16_t* row = a.rows + (int64_t)r * a.pitch;
-          pacc ^= row[d];
-          const int64_t c = mod_s(d - r, S);
-          if (a.excl[r] == d) continue;  // c == star_r
-          qacc ^= row[c];
+          const int64_t c = wrap_s(d - r, S);
+          const uint16_t pw = row[d], qw = row[c];
+          pacc ^= pw;
+          qacc ^= a.excl[r] == d ? (uint16_t)0 : qw;  // c == star_r: skipped
         }
         prow[d] = pacc;
         qrow[d] = qacc;
       }
+    }
+  }
+}
+
+// Any row alignment (pitch not a multiple of 8 words, or an unaligned base):
+// P and Q are written with aligned 16-byte stores of their own rows (work item
+// g < np covers a P vector, the rest Q vectors); every row is read through
+// ldu16 windows (P at d0, Q at d0 - r). Unaligned heads, the wrapping start of
+// Q (d0 < nd - 1) and partial tails use the scalar formula.
+__device__ __forceinline__ void ref_words(const RdpRefParityArgs& a, int64_t d, uint16_t* pw, uint16_t* qw) {
+  uint16_t pacc = 0, qacc = 0;
+#pragma unroll
+  for (int r = 0; r < kRefMaxNd; ++r) {  // loads independent of each other
+    if (r >= a.nd) break;
+    const uint16_t* row = a.rows + (int64_t)r * a.pitch;
+    const int64_t c = wrap_s(d - r, a.S);
+    const uint16_t p = row[d], q = row[c];
+    pacc ^= p;
+    qacc ^= a.excl[r] == d ? (uint16_t)0 : q;
+  }
+  if (pw) *pw = pacc;
+  if (qw) *qw = qacc;
+}
+
+__global__ void __launch_bounds__(256) rdpref_parity_any(RdpRefParityArgs a) {
+  const int64_t S = a.S;
+  const int64_t slots = (S >> 3) + 2;
+  uint16_t* prow = a.rows + (int64_t)a.nd * a.pitch;
+  uint16_t* qrow = a.rows + (int64_t)(a.nd + 1) * a.pitch;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < 2 * slots; g += (int64_t)gridDim.x * blockDim.x) {
+    const bool isp = g < slots;
+    uint16_t* out = isp ? prow : qrow;
+    const int64_t j = isp ? g : g - slots;
+    int64_t h = ((16 - (int64_t)(reinterpret_cast<uintptr_t>(out) & 15u)) & 15) >> 1;
+    if (h > S) h = S;
+    const int64_t d0 = j == 0 ? 0 : h + (j - 1) * 8;
+    const int64_t d1 = j == 0 ? h : (d0 + 8 < S ? d0 + 8 : S);
+    if (d0 >= d1) continue;
+    const bool full = d1 - d0 == 8;
+    if (isp && full) {
+      uint4 acc = vzero();
+      for (int r = 0; r < a.nd; ++r) acc = vxor(acc, ldu16(a.rows + (int64_t)r * a.pitch + d0));
+      *reinterpret_cast<uint4*>(out + d0) = acc;
+    } else if (!isp && full && d0 >= (int64_t)(a.nd - 1)) {
+      uint4 acc = vzero();
+      for (int r = 0; r < a.nd; ++r) {
+        uint4 win = ldu16(a.rows + (int64_t)r * a.pitch + d0 - r);
+        const int64_t ex = a.excl[r];
+        if (ex >= d0 && ex < d0 + 8) win = clear_lane(win, (int)(ex - d0));
+        acc = vxor(acc, win);
+      }
+      *reinterpret_cast<uint4*>(out + d0) = acc;
+    } else {
+      for (int64_t d = d0; d < d1; ++d) ref_words(a, d, isp ? out + d : nullptr, isp ? nullptr : out + d);
     }
   }
 }
@@ -139,13 +208,29 @@ int rdpref_parity(uint16_t* rows, int64_t pitch, int nd, int64_t S, int star_bas
     a.excl[r] = sr < 0 ? -1 : (int64_t)((sr + r) % S);
   }
   a.vec_ok = aligned16(rows) && (pitch % 8 == 0);
-  const int64_t nvec = (S + 7) >> 3;
   const int threads = 256;
+  if (!a.vec_ok) {
+    int64_t grid = (2 * ((S >> 3) + 2) + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    grid = grid > cap ? cap : (grid < 1 ? 1 : grid);
+    rdpref_parity_any<<<(int)grid, threads, 0, s>>>(a);
+    return check_launch("rdpref_parity_any");
+  }
+  const int64_t nvec = (S + 7) >> 3;
   int64_t grid = (nvec + threads - 1) / threads;
   const int64_t cap = (int64_t)sm_count() * 8;
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
-  rdpref_parity_kernel<<<(int)grid, threads, 0, s>>>(a);
+  switch (nd) {
+    case 2: rdpref_parity_kernel<2><<<(int)grid, threads, 0, s>>>(a); break;
+    case 3: rdpref_parity_kernel<3><<<(int)grid, threads, 0, s>>>(a); break;
+    case 4: rdpref_parity_kernel<4><<<(int)grid, threads, 0, s>>>(a); break;
+    case 5: rdpref_parity_kernel<5><<<(int)grid, threads, 0, s>>>(a); break;
+    case 6: rdpref_parity_kernel<6><<<(int)grid, threads, 0, s>>>(a); break;
+    case 7: rdpref_parity_kernel<7><<<(int)grid, threads, 0, s>>>(a); break;
+    case 8: rdpref_parity_kernel<8><<<(int)grid, threads, 0, s>>>(a); break;
+    default: rdpref_parity_kernel<0><<<(int)grid, threads, 0, s>>>(a); break;
+  }
   return check_launch("rdpref_parity_kernel");
 }
 

@@ -352,3 +352,69 @@ def test_live_reference_hook(rng):
     e.rdp_kv_ops.compute_rdp_parity(r2, nd=world, S=S, star_base=0)
     torch.cuda.synchronize()
     assert torch.equal(r1, r2)
+
+
+# ------------------------------------------- unaligned caller layouts -------
+# The reference's extension calls take [rows, S] tensors whose rows start at
+# any byte offset; these sizes put every row (and the parity rows) at a
+# different misalignment, large enough for the vector paths with ldu16 windows.
+@pytest.mark.parametrize("s", [4793491, 200003, 65536 + 7])
+@pytest.mark.parametrize("k", [2, 3, 7])
+def test_unaligned_xor_extension_calls(rng, s, k):
+    e = pkg("ext")
+    dp_np = rng.integers(0, 256, k * s, dtype=np.uint8)
+    dp = torch.from_numpy(dp_np).cuda()
+    sh = torch.zeros((k + 1, s), dtype=torch.uint8, device="cuda")
+    e.xor_kernel.encode_xor(dp, sh, k, s)
+    want = R.xor_encode(dp_np, k, s)
+    assert np.array_equal(sh.cpu().numpy(), want)
+    miss = k // 2
+    rec = torch.empty((1, s), dtype=torch.uint8, device="cuda")
+    broken = sh.clone()
+    broken[miss].zero_()
+    e.xor_kernel.reconstruct_xor(broken, broken, rec, s, k, torch.tensor([miss], dtype=torch.int32, device="cuda"))
+    assert torch.equal(broken, sh)
+
+
+@pytest.mark.parametrize("nd,star", [(6, 0), (5, 3), (8, 1)])
+@pytest.mark.parametrize("T,n", [(257, 40), (1024, 136)])
+def test_unaligned_rdpref_extension_calls(rng, nd, star, T, n):
+    e = pkg("ext")
+    k_np, v_np = fp16_bits(rng, (T, n)), fp16_bits(rng, (T, n))
+    S, _ = R.determine_shard_size_words(2 * T * n, nd)
+    sh = torch.zeros((nd + 2, S), dtype=torch.uint16, device="cuda")  # rows 2*S bytes apart: any alignment
+    kt = torch.from_numpy(k_np).cuda().view(torch.float16)
+    vt = torch.from_numpy(v_np).cuda().view(torch.float16)
+    e.rdp_kernel.fused_backup_full_kv(kt, vt, sh, nd, S, T, n, star)
+    rows = R.rdpref_pack(k_np, v_np, nd, S)
+    want = R.rdpref_parity(rows, nd, S, star)
+    assert np.array_equal(sh.cpu().numpy(), want)
+    out = torch.empty(2 * T * n, dtype=torch.float16, device="cuda")
+    broken = sh.clone()
+    broken[1].zero_()
+    e.rdp_kernel.fused_recovery_full_kv(broken, out, nd, S, T, n, star, 1, -1)
+    assert np.array_equal(out.view(torch.int16).cpu().numpy().view(np.uint16),
+                          np.concatenate([k_np.reshape(-1), v_np.reshape(-1)]))
+
+
+@pytest.mark.parametrize("k,m,s", [(6, 2, 100003), (3, 3, 65536 + 5), (8, 2, 4099)])
+def test_unaligned_rs16_extension_calls(rng, k, m, s):
+    e = pkg("ext")
+    dp_np = rng.integers(0, 1 << 16, k * s, dtype=np.uint16)
+    sh = torch.zeros((k + m, s), dtype=torch.uint16, device="cuda")
+    e.rs_kernel.encode_rs_u16(torch.from_numpy(dp_np).cuda(), sh, k, m, s)
+    assert np.array_equal(sh.cpu().numpy(), R.rs16_encode(dp_np, k, m, s))
+
+
+@pytest.mark.parametrize("B,H,T,D", [(1, 3, 129, 40), (2, 2, 300, 128), (1, 1, 1000, 12)])
+def test_unaligned_bhtd_layouts(rng, B, H, T, D):
+    r = pkg("benchmark.rdp.main")
+    k_np, v_np = fp16_bits(rng, (B, H, T, D)), fp16_bits(rng, (B, H, T, D))
+    kt = torch.from_numpy(k_np).cuda().view(torch.float16)
+    vt = torch.from_numpy(v_np).cuda().view(torch.float16)
+    for nd in (5, 7):
+        p = r.fused_backup_full_kv(kt, vt, nd, star_base=2)
+        enc, S, _ = R.rdpref_backup(k_np, v_np, nd, 2)
+        assert np.array_equal(u16(p["shards_KV"]), enc)
+        ko, vo, _ = r.fused_recovery_full_kv(p, 2)
+        assert np.array_equal(u16(ko), k_np) and np.array_equal(u16(vo), v_np)
