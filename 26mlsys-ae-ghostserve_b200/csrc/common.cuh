@@ -88,6 +88,21 @@ class LaunchCache {
 // The process-wide cache.
 LaunchCache& launch_cache();
 
+// Division of 32-bit values by a run-time constant d (1 <= d < 2^32), with the
+// multiplier precomputed on the host (Granlund-Montgomery, round-up variant):
+// s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1, q = (umulhi(x, m) + x) >> s.
+struct FastDiv {
+  uint32_t d = 1, m = 1, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div) {
+    while ((1ull << s) < div) ++s;
+    m = (uint32_t)(((((1ull << s) - div) << 32) / div) + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t x) const {
+    return (uint32_t)((((uint64_t)__umulhi(x, m)) + x) >> s);
+  }
+};
+
 // ---------------------------------------------------------- vector access ---
 
 __device__ __forceinline__ uint4 vxor(uint4 a, uint4 b) {

@@ -144,12 +144,40 @@ __global__ void rows_unpack_any(const char* rows, int64_t pitch, int64_t row_byt
 // t = j / n, c = j % n, bh = c / D, d = c % D; source word (bh*T + t)*D + d.
 struct Perm {
   int64_t T, D, n, Tn;
+  bool small;                  // every stream/source index and row slot fits 32 bits: fast division
+  FastDiv fn, fD, fT, fslots;  // by n, D, T and the row-slot count of the *_any kernels
 };
 
+Perm make_perm(int64_t B, int64_t H, int64_t T, int64_t D, int64_t slots) {
+  Perm p{T, D, B * H * D, T * B * H * D, false, FastDiv(), FastDiv(), FastDiv(), FastDiv()};
+  p.small = 2 * p.Tn + 64 < (1ll << 31) && slots < (1ll << 31);
+  if (p.small) {
+    p.fn = FastDiv((uint32_t)p.n);
+    p.fD = FastDiv((uint32_t)D);
+    p.fT = FastDiv((uint32_t)T);
+    p.fslots = FastDiv((uint32_t)(slots > 0 ? slots : 1));
+  }
+  return p;
+}
+
 __device__ __forceinline__ int64_t perm_src(const Perm& p, int64_t j) {
+  if (p.small) {
+    const uint32_t jj = (uint32_t)j, t = p.fn.div(jj), c = jj - t * (uint32_t)p.n;
+    const uint32_t bh = p.fD.div(c), d = c - bh * (uint32_t)p.D;
+    return (int64_t)((bh * (uint32_t)p.T + t) * (uint32_t)p.D + d);
+  }
   const int64_t t = j / p.n, c = j - t * p.n;
   const int64_t bh = c / p.D, d = c - bh * p.D;
   return (bh * p.T + t) * p.D + d;
+}
+
+// (word d within its run of D, and the run's token-major stream index) helpers
+__device__ __forceinline__ int64_t perm_d(const Perm& p, int64_t j) {
+  if (p.small) {
+    const uint32_t jj = (uint32_t)j, t = p.fn.div(jj), c = jj - t * (uint32_t)p.n;
+    return (int64_t)(c - p.fD.div(c) * (uint32_t)p.D);
+  }
+  return (j % p.n) % p.D;
 }
 
 // Vector path needs D % 8 == 0, S % 8 == 0, aligned rows/pitch/tensors: then a
@@ -209,7 +237,7 @@ __global__ void bhtd_pack_any(const uint16_t* k, const uint16_t* v, Perm p, uint
   const int64_t slots = (S >> 3) + 2;
   const int64_t total = slots * nd;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = g / slots, j = g - r * slots;
+    const int64_t r = p.small ? (int64_t)p.fslots.div((uint32_t)g) : g / slots, j = g - r * slots;
     uint16_t* base = rows + r * pitch;
     int64_t h = ((16 - (int64_t)(reinterpret_cast<uintptr_t>(base) & 15u)) & 15) >> 1;  // words
     if (h > S) h = S;
@@ -223,10 +251,27 @@ __global__ void bhtd_pack_any(const uint16_t* k, const uint16_t* v, Perm p, uint
         stv(base + c0, vzero());
         done = true;
       } else if (i0 + 8 <= p.Tn || (i0 >= p.Tn && i0 + 8 <= 2 * p.Tn)) {
+        const uint16_t* src = i0 < p.Tn ? k : v;
         const int64_t jj = i0 < p.Tn ? i0 : i0 - p.Tn;
-        const int64_t t = jj / p.n, c = jj - t * p.n, d = c % p.D;
+        const int64_t d = perm_d(p, jj);
         if (d + 8 <= p.D) {
-          stv(base + c0, ldu16((i0 < p.Tn ? k : v) + perm_src(p, jj)));
+          stv(base + c0, ldu16(src + perm_src(p, jj)));
+          done = true;
+        } else if (p.D >= 8) {
+          // the 8 words straddle two runs of D: the first kk words end run A, the
+          // rest start run B; B is read as a window starting kk words early and
+          // its first kk words are replaced by A's
+          const int kk = (int)(p.D - d);
+          const uint4 a = ldu16(src + perm_src(p, jj));
+          const uint4 b = ldu16(src + perm_src(p, jj + kk) - kk);
+          const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int l = 0; l < 4; ++l) {  // words 2l, 2l+1 of the result
+            const uint32_t m = (2 * l + 1 < kk) ? 0xffffffffu : (2 * l < kk ? 0x0000ffffu : 0u);
+            o[l] = (av[l] & m) | (bv[l] & ~m);
+          }
+          stv(base + c0, make_uint4(o[0], o[1], o[2], o[3]));
           done = true;
         }
       }
@@ -252,7 +297,17 @@ __global__ void bhtd_unpack_any(const uint16_t* rows, int64_t pitch, int64_t S, 
     const int64_t w1 = j == 0 ? h : (w0 + 8 < p.Tn ? w0 + 8 : p.Tn);
     if (w0 >= w1) continue;
     // destination word w = ((bh * T + t) * D + d)  ->  stream word t * n + bh * D + d
-    const int64_t d = w0 % p.D, bt = w0 / p.D, t = bt % p.T, bh = bt / p.T;
+    int64_t d, t, bh;
+    if (p.small) {
+      const uint32_t bt = p.fD.div((uint32_t)w0), b2 = p.fT.div(bt);
+      d = (int64_t)((uint32_t)w0 - bt * (uint32_t)p.D);
+      t = (int64_t)(bt - b2 * (uint32_t)p.T);
+      bh = (int64_t)b2;
+    } else {
+      d = w0 % p.D;
+      t = (w0 / p.D) % p.T;
+      bh = (w0 / p.D) / p.T;
+    }
     const int64_t i = toff + t * p.n + bh * p.D + d;
     const int64_t r = i / S, x = i - r * S;
     if (w1 - w0 == 8 && d + 8 <= p.D && x + 8 <= S && (reinterpret_cast<uintptr_t>(dst + w0) & 15u) == 0) {
@@ -314,7 +369,8 @@ int rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int nrows, v
 int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_t T, int64_t D, uint16_t* rows,
               int64_t pitch, int nd, int64_t S, cudaStream_t s) {
   GSEC_REQUIRE(k && v && rows && B >= 1 && H >= 1 && T >= 1 && D >= 1 && nd >= 1, "bhtd_pack: bad args");
-  Perm p{T, D, B * H * D, T * B * H * D};
+  Perm p = make_perm(B, H, T, D, (S >> 3) + 2);
+  if (((S >> 3) + 2) * nd >= (1ll << 31)) p.small = false;  // slot indices past 32 bits
   GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_pack: rows too small");
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
@@ -329,7 +385,7 @@ int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_
 int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t* k, uint16_t* v, int64_t B,
                 int64_t H, int64_t T, int64_t D, cudaStream_t s) {
   GSEC_REQUIRE(k && v && rows && B >= 1 && H >= 1 && T >= 1 && D >= 1 && nd >= 1, "bhtd_unpack: bad args");
-  Perm p{T, D, B * H * D, T * B * H * D};
+  Perm p = make_perm(B, H, T, D, 1);
   GSEC_REQUIRE(S * nd >= 2 * p.Tn && pitch >= S, "bhtd_unpack: rows too small");
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
