@@ -636,6 +636,7 @@ def run_sweep(args):
                         src = torch.empty(nbytes, dtype=torch.uint8, device=device)
                         g._lib.call("gsec_copy_async", g._lib.C.c_void_p(src.data_ptr()), g._lib.C.c_void_p(data[e]),
                                     nbytes, g._lib.C.c_void_p(sh))
+                        torch.cuda.synchronize()  # the copy ran on the capture stream
                         flags += 0 if torch.equal(src, t) else 1
                     dist.all_reduce(flags)
                     ok = int(flags.item()) == 0
