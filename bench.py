@@ -206,7 +206,7 @@ def run_reference(args, wl):
     nbytes = data[0].size
     for _ in range(args.warmup):
         cpu_encode_rate(wl, data, 0.0, max_reps=1)
-    rate, reps, threads, el = cpu_encode_rate(wl, data, 0.0, max_reps=args.steps)
+    rate, reps, threads, el = cpu_encode_rate(wl, data, float("inf"), max_reps=args.steps)  # exactly K steps
     sample = f"{wl['k']} x {nbytes} B shards per step ({nbytes / wl['shard']:.3f} of the workload), {reps} steps"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(rate, 3), "unit": "GB/s", "n_gpus": args.gpus,
