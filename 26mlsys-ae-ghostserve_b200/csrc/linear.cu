@@ -164,9 +164,9 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
 }
 
 template <int SPS>
-int launch_xor(const LinearPass& a, cudaStream_t s) {
-  // keep ~18 KiB of loads in flight per CTA whatever the input count
-  int nst = kLRingBytes / (a.nin * SPS * kLSeg);
+int launch_xor(const LinearPass& a, cudaStream_t s, int ring_bytes) {
+  // keep ring_bytes of loads in flight per CTA whatever the input count
+  int nst = ring_bytes / (a.nin * SPS * kLSeg);
   nst = nst < kLStages ? kLStages : (nst > 18 ? 18 : nst);
   LaunchCache& cache = launch_cache();
   auto k = xor_tma_kernel<SPS>;
@@ -581,7 +581,10 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
   if (!pass_aligned(a)) return run_unaligned(a, s);
   switch (a.field) {
     case Field::XOR:
-      return a.nin <= 1 ? launch_xor<4>(a, s) : (a.nin <= 3 ? launch_xor<2>(a, s) : launch_xor<1>(a, s));
+      // measured: 2-3 inputs run best with 4 KiB stages and a 36 KiB ring, one
+      // input with 4 KiB stages and the default ring, more inputs with 1 KiB stages
+      return a.nin <= 1 ? launch_xor<4>(a, s, kLRingBytes)
+                        : (a.nin <= 3 ? launch_xor<4>(a, s, 2 * kLRingBytes) : launch_xor<1>(a, s, kLRingBytes));
     case Field::GF8: {
       switch (a.nin) {
         case 1: return launch_gf8_fixed<1>(a, s);
