@@ -40,11 +40,10 @@ __device__ __forceinline__ void st16(char* p, uint4 v) {
                : "memory");
 }
 
-// Bytes [t0, t1) of every output (a pass's unaligned head or sub-vector tail),
-// one thread, symbol at a time.
-__device__ void linear_range(const LinearPass& a, int64_t t0, int64_t t1) {
+// Sub-vector tail [t0, end) of every output, one thread, symbol at a time.
+__device__ void linear_tail(const LinearPass& a, int64_t t0) {
   if (a.field == Field::GF16) {
-    for (int64_t x = t0; x + 2 <= t1; x += 2) {
+    for (int64_t x = t0; x + 2 <= a.end; x += 2) {
       for (int j = 0; j < a.nout; ++j) {
         uint32_t acc = 0;
         for (int i = 0; i < a.nin; ++i) {
@@ -57,7 +56,7 @@ __device__ void linear_range(const LinearPass& a, int64_t t0, int64_t t1) {
     }
     return;
   }
-  for (int64_t x = t0; x < t1; ++x) {
+  for (int64_t x = t0; x < a.end; ++x) {
     for (int j = 0; j < a.nout; ++j) {
       uint32_t acc = 0;
       for (int i = 0; i < a.nin; ++i) {
@@ -67,11 +66,6 @@ __device__ void linear_range(const LinearPass& a, int64_t t0, int64_t t1) {
       if (x < a.out_end[j]) *reinterpret_cast<uint8_t*>(seg(a.out_lo[j], a.out_hi[j], a.split, x)) = (uint8_t)acc;
     }
   }
-}
-
-__device__ __forceinline__ void linear_tail(const LinearPass& a, int64_t t0) {
-  linear_range(a, t0, a.end);
-  if (a.head > 0) linear_range(a, a.begin - a.head, a.begin);
 }
 
 // ------------------------------------------------------- XOR (TMA ring) -----
@@ -548,13 +542,14 @@ int run_unaligned(const LinearPass& a, cudaStream_t s) {
     int64_t x = a.begin;
     while (((reinterpret_cast<uintptr_t>(b.out_lo[0]) + (uintptr_t)x) & 15u) && x < a.end) ++x;
     if (a.field == Field::GF16 && ((x - a.begin) & 1)) return run_scalar(a, s);  // odd byte output base
-    if (x >= a.end) {
-      const int rc = run_scalar(b, s);
+    if (x > a.begin) {  // the bytes before the first aligned output address
+      LinearPass h = b;
+      h.end = x < a.end ? x : a.end;
+      const int rc = run_scalar(h, s);
       if (rc) return rc;
-      continue;
     }
+    if (x >= a.end) continue;
     b.begin = x;
-    b.head = x - a.begin;  // done by the vector kernel's first thread with its tail
     int rc;
     if (a.field == Field::XOR) {
       const int threads = 256;

@@ -26,7 +26,6 @@ struct LinearPass {
   int64_t begin;      // byte offset, multiple of 16
   int64_t end;        // byte offset (may have a sub-16-byte tail)
   int64_t out_end[kLinMaxOut];  // an output is written only below this offset
-  int64_t head;       // bytes before begin done one symbol at a time (0 unless set)
   uint16_t coef[kLinMaxOut][kLinMaxIn];  // GF8 uses the low byte; XOR ignores
   int nin;
   int nout;
