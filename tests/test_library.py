@@ -139,3 +139,35 @@ def test_engine_requires_cuda_tensors():
     g = pkg()
     with pytest.raises(ValueError, match="CUDA"):
         g.encode(g.CodeSpec.xor(2), [torch.zeros(32, dtype=torch.uint8)] * 2)
+
+
+def test_slot_and_copy_argument_checks_run_on_host():
+    L = pkg("_lib")
+    P = ctypes.c_void_p
+    # slot list element size
+    with pytest.raises(ValueError, match="slot_bytes"):
+        L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 256, P(0x20000), 3, 4, 64, P(0x30000), None)
+    # null pool / destination
+    with pytest.raises(ValueError, match="null"):
+        L.call("gsec_slots_gather", None, 512, 256, 1, 256, P(0x20000), 8, 4, 64, P(0x30000), None)
+    with pytest.raises(ValueError, match="null"):
+        L.call("gsec_slots_scatter", P(0x10000), 512, 256, 1, 256, P(0x20000), 8, 4, 64, None, None)
+    # rows that are not whole 16-byte vectors
+    with pytest.raises(ValueError, match="16-byte"):
+        L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 200, P(0x20000), 8, 4, 64, P(0x30000), None)
+    # an empty slot list is a no-op, even with no list pointer
+    L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 256, None, 8, 0, 64, P(0x30000), None)
+    with pytest.raises(ValueError):
+        L.call("gsec_copy_async", P(0x10000), P(0x20000), -1, None)
+    with pytest.raises(ValueError, match="null"):
+        L.call("gsec_copy_async", None, P(0x20000), 16, None)
+    L.call("gsec_copy_async", None, None, 0, None)  # nothing to copy
+
+
+def test_slots_gather_rejects_host_tensors():
+    import torch
+
+    c = pkg("codec")
+    pool = torch.zeros(8, 2, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        c.slots_gather(pool, torch.arange(4), torch.empty(4096, dtype=torch.uint8))
