@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bf16_bits, pkg, rand_bytes
+from conftest import pkg, rand_bytes
 from oracle import codes
 
 pytestmark = pytest.mark.gpu
