@@ -449,12 +449,24 @@ int gsec_rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int32_t
   return rows_unpack(rows, pitch, row_bytes, nrows, dst0, len0, dst1, len1, as_stream(stream));
 }
 
+namespace {
+// Every plane of a slot's record must lie inside the record: planes at byte
+// offsets 0, plane, ..., (nplanes-1)*plane, each row_bytes long, in pitch bytes.
+bool slot_geometry_ok(int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes) {
+  if (pitch <= 0 || plane < 0 || row_bytes <= 0 || nplanes < 1) return false;
+  if (plane > 0 && (int64_t)(nplanes - 1) > (pitch - row_bytes) / plane) return false;
+  return (int64_t)(nplanes - 1) * plane + row_bytes <= pitch;
+}
+}  // namespace
+
 int gsec_slots_gather(const void* pool, int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes,
                       const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows, void* dst,
                       gsec_stream_t stream) {
   GSEC_REQUIRE(pool != nullptr && dst != nullptr && (n == 0 || slots != nullptr), "null pointer");
   GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
   GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
+  GSEC_REQUIRE(slot_geometry_ok(pitch, plane, nplanes, row_bytes),
+               "slot record: need pitch > 0, plane >= 0 and (nplanes-1)*plane + row_bytes <= pitch");
   return slots_move(true, const_cast<void*>(pool), pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
                     dst, as_stream(stream));
 }
@@ -465,6 +477,8 @@ int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_t nplanes
   GSEC_REQUIRE(pool != nullptr && src != nullptr && (n == 0 || slots != nullptr), "null pointer");
   GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
   GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
+  GSEC_REQUIRE(slot_geometry_ok(pitch, plane, nplanes, row_bytes),
+               "slot record: need pitch > 0, plane >= 0 and (nplanes-1)*plane + row_bytes <= pitch");
   return slots_move(false, pool, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
                     const_cast<void*>(src), as_stream(stream));
 }

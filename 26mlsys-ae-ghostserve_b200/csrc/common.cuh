@@ -38,6 +38,23 @@ int sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+#ifndef GSEC_BALANCED_GRID
+#define GSEC_BALANCED_GRID 1
+#endif
+// Grid for `items` equal work items handed out round-robin (item it to CTA
+// it % grid), at most `max_grid` CTAs: the fewest CTAs that still finish in
+// the same number of rounds, so every CTA gets either ceil(items / grid) or
+// one item fewer, and no last round runs with a fraction of the CTAs while
+// the rest sit idle (5464 items on 740 resident CTAs: 683 CTAs x 8 items).
+inline int64_t balanced_grid(int64_t items, int64_t max_grid) {
+  if (items < 1) return 1;
+  if (max_grid < 1) max_grid = 1;
+  if (items <= max_grid) return items;
+  if (!GSEC_BALANCED_GRID) return max_grid;
+  const int64_t rounds = (items + max_grid - 1) / max_grid;
+  return (items + rounds - 1) / rounds;
+}
+
 // Per-device cache of kernels' launch shapes: a kernel's dynamic shared
 // memory attribute is raised once and its resident-CTA count is queried once
 // per (device, kernel, shared-memory size), instead of on every launch.

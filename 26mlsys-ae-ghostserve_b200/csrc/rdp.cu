@@ -422,8 +422,7 @@ int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
     if (per_sm < 0) return check_launch("rdp_encode_tma launch shape");
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
-    int64_t grid = (int64_t)sm_count() * per_sm;
-    if (grid > items) grid = items;
+    const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
     k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, nst);
     return check_launch("rdp_encode_tma_kernel");
   }
@@ -447,8 +446,7 @@ int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
     if (per_sm < 0) return check_launch("rdp_decode_tma launch shape");
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
-    int64_t grid = (int64_t)sm_count() * per_sm;
-    if (grid > items) grid = items;
+    const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
     k<<<(int)grid, kDecThreads, smem, s>>>(a, nst);
     return check_launch("rdp_decode_tma_kernel");
   }

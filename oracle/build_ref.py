@@ -31,7 +31,10 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
-REF_ROOT_DEFAULT = "/".join(["", "root", "reference"])
+# The reference checkout: $GSEC_REFERENCE_ROOT, else a directory named
+# "reference" beside this repository's root.
+REF_ROOT_DEFAULT = os.environ.get("GSEC_REFERENCE_ROOT") or os.path.normpath(
+    os.path.join(HERE, os.pardir, os.pardir, "reference"))
 
 # (module name, source path relative to the reference root or None for the hook string, cuda flags)
 REF_EXTS = {

@@ -278,3 +278,70 @@ def hook_pool(rank, world, port, backend, out):
     dist.all_gather_object(oks, ok)
     out.put((rank, all(oks), [r["chunk_id"] for r in ft.records]))
     dist.destroy_process_group()
+
+
+def hook_reference(rank, world, port, backend, out):
+    """The hook in mode="reference" as SGLang drives it: a FlashInfer-like
+    backend's extend calls go through on_extend (active slots, chunk-id
+    broadcast, NCCL gather to the rotating rank, fp16 cast, pack, mod-S parity,
+    host copy). The destination rank's P/Q must equal what the reference's own
+    rdp_kv_ops extension computes from the same gathered rows."""
+    _init(rank, world, port, backend)
+    torch.cuda.set_device(rank)
+    hook = _pkg("hook")
+    from oracle import build_ref
+
+    if not build_ref.built("rdp_kv_ops"):
+        out.put((rank, "skip", []))
+        dist.destroy_process_group()
+        return
+    ref = build_ref.load_ref("rdp_kv_ops")
+
+    class FlashInferAttnBackend:
+        def __init__(self):
+            g = torch.Generator(device="cuda").manual_seed(200 + rank)
+            self.kv_buffer = torch.randn(512, 2, 1, 128, device="cuda", generator=g).to(torch.bfloat16)
+
+        def forward_extend(self, batch, layer=None, save_kv_cache=True):
+            return "attn-out"
+
+    class Batch:
+        def __init__(self, slot_mapping):
+            self.slot_mapping = slot_mapping
+
+    be = FlashInferAttnBackend()
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="reference", star_base=1, metrics_file=None))
+    seen = []
+    real = ft.compute_parity_to_cpu
+
+    def capture(K_all, V_all, elems, chunk_id, dst_rank):
+        P, Q = real(K_all, V_all, elems, chunk_id, dst_rank)
+        seen.append((K_all.clone(), V_all.clone(), elems, P, Q))
+        return P, Q
+
+    ft.compute_parity_to_cpu = capture
+    assert hook.patch_backend(be, ft)
+    gen = torch.Generator().manual_seed(9)  # the same slot lists on every rank
+    ok = True
+    for n in (64, 40, 200):
+        perm = torch.randperm(512, generator=gen)[:n]
+        perm[torch.randperm(n, generator=gen)[: n // 8]] = -1
+        assert be.forward_extend(Batch(perm.cuda()), layer=0) == "attn-out"
+        torch.cuda.synchronize()
+    for K_all, V_all, elems, P, Q in seen:
+        S = 2 * elems
+        rows = torch.empty((world + 2, S), dtype=torch.uint16, device="cuda")
+        for r in range(world):
+            k = K_all.narrow(0, r * elems, elems).to(torch.float16)
+            v = V_all.narrow(0, r * elems, elems).to(torch.float16)
+            ref.pack_row_from_block(k.view(1, 1, elems, 1), v.view(1, 1, elems, 1), rows, r)
+        ref.compute_rdp_parity(rows, nd=world, S=S, star_base=1)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(rows[world].cpu(), P) and torch.equal(rows[world + 1].cpu(), Q)
+    # the gathered rows are the active slots' K and V of every rank, in rank order
+    recs = [(r["chunk_id"], r["dst_rank"]) for r in ft.records]
+    ft.close()
+    oks = [None] * world
+    dist.all_gather_object(oks, (ok, len(seen)))
+    out.put((rank, oks, recs))
+    dist.destroy_process_group()

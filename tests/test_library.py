@@ -142,6 +142,8 @@ def test_engine_requires_cuda_tensors():
 
 
 def test_slot_and_copy_argument_checks_run_on_host():
+    """Calls that fail on the first null-pointer or size check, before any later
+    check could let them reach a launch: the fake addresses are never used."""
     L = pkg("_lib")
     P = ctypes.c_void_p
     # slot list element size
@@ -152,16 +154,35 @@ def test_slot_and_copy_argument_checks_run_on_host():
         L.call("gsec_slots_gather", None, 512, 256, 1, 256, P(0x20000), 8, 4, 64, P(0x30000), None)
     with pytest.raises(ValueError, match="null"):
         L.call("gsec_slots_scatter", P(0x10000), 512, 256, 1, 256, P(0x20000), 8, 4, 64, None, None)
-    # rows that are not whole 16-byte vectors
-    with pytest.raises(ValueError, match="16-byte"):
-        L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 200, P(0x20000), 8, 4, 64, P(0x30000), None)
-    # an empty slot list is a no-op, even with no list pointer
-    L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 256, None, 8, 0, 64, P(0x30000), None)
     with pytest.raises(ValueError):
         L.call("gsec_copy_async", P(0x10000), P(0x20000), -1, None)
     with pytest.raises(ValueError, match="null"):
         L.call("gsec_copy_async", None, P(0x20000), 16, None)
     L.call("gsec_copy_async", None, None, 0, None)  # nothing to copy
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="fake device addresses: host-only machine")
+def test_slot_record_checks_run_on_host():
+    """Alignment, record geometry and the empty list: checks that come after
+    the null/size checks. With a GPU present a loosened check could launch on
+    the fake addresses, so these run only where no GPU exists."""
+    L = pkg("_lib")
+    P = ctypes.c_void_p
+    # rows that are not whole 16-byte vectors
+    with pytest.raises(ValueError, match="16-byte"):
+        L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 200, P(0x20000), 8, 4, 64, P(0x30000), None)
+    # planes that do not fit in the slot record, negative plane offset, zero pitch
+    for fn in ("gsec_slots_gather", "gsec_slots_scatter"):
+        with pytest.raises(ValueError, match="slot record"):
+            L.call(fn, P(0x10000), 512, 256, 2, 512, P(0x20000), 8, 4, 64, P(0x30000), None)
+        with pytest.raises(ValueError, match="slot record"):
+            L.call(fn, P(0x10000), 512, -256, 2, 256, P(0x20000), 8, 4, 64, P(0x30000), None)
+        with pytest.raises(ValueError, match="slot record"):
+            L.call(fn, P(0x10000), 0, 0, 1, 256, P(0x20000), 8, 4, 64, P(0x30000), None)
+        with pytest.raises(ValueError, match="slot record"):
+            L.call(fn, P(0x10000), 512, 1 << 62, 3, 256, P(0x20000), 8, 4, 64, P(0x30000), None)
+    # an empty slot list is a no-op, even with no list pointer
+    L.call("gsec_slots_gather", P(0x10000), 512, 256, 1, 256, None, 8, 0, 64, P(0x30000), None)
 
 
 def test_slots_gather_rejects_host_tensors():
