@@ -66,6 +66,7 @@ _SIGS = {
     "gsec_rows_pack": (C.c_int, [_P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P]),
     "gsec_rows_unpack": (C.c_int, [_P, _I64, _I64, _I32, _P, _I64, _P, _I64, _P]),
     "gsec_copy_async": (C.c_int, [_P, _P, _I64, _P]),
+    "gsec_copy_gather": (C.c_int, [_PP, C.POINTER(_I64), _I32, _P, _P]),
     "gsec_slots_gather": (C.c_int, [_P, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P]),
     "gsec_slots_scatter": (C.c_int, [_P, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P]),
     "gsec_xor_encode": (C.c_int, [_P, _P, _I32, _I64, _I64, _P]),

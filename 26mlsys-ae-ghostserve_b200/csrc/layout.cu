@@ -449,6 +449,69 @@ __global__ void slots_scatter_vec(char* pool, int64_t pitch, int64_t plane, int 
 }
 }  // namespace
 
+// --------------------------------------------------- gather of n buffers --
+// dst = src[0][0..bytes[0]) ++ src[1][0..bytes[1]) ++ ... with 16-byte loads,
+// four in flight per thread. The sources may be mapped peer buffers, so this
+// is also the plain peer-read copy that bench.py times as the NVLink ceiling of
+// a placement (the encode kernels read the same bytes with bulk copies).
+namespace {
+constexpr int kGatherMax = 32;
+struct GatherArgs {
+  const char* src[kGatherMax];
+  int64_t vend[kGatherMax];  // cumulative 16-byte vector counts
+  int n;
+  char* dst;
+};
+
+__device__ __forceinline__ const char* gather_src(const GatherArgs& a, int64_t v) {
+  int i = 0;
+  while (i + 1 < a.n && v >= a.vend[i]) ++i;
+  return a.src[i] + ((v - (i ? a.vend[i - 1] : 0)) << 4);
+}
+
+__global__ void __launch_bounds__(256) gather_vec(const GatherArgs a) {
+  const int64_t total = a.vend[a.n - 1];
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += 4 * step) {
+    uint4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v + u * step < total) x[u] = ldv(gather_src(a, v + u * step));
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v + u * step < total) stv(a.dst + ((v + u * step) << 4), x[u]);
+  }
+}
+}  // namespace
+
+int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, cudaStream_t s) {
+  if (n < 1 || n > kGatherMax) {
+    set_error("gather: 1..%d sources", kGatherMax);
+    return GSEC_EINVAL;
+  }
+  GatherArgs a{};
+  a.n = n;
+  a.dst = static_cast<char*>(dst);
+  int64_t acc = 0;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] < 0 || (bytes[i] & 15) || (bytes[i] && (!src[i] || !aligned16(src[i])))) {
+      set_error("gather: source %d must be 16-byte aligned with a size that is a multiple of 16", i);
+      return GSEC_EINVAL;
+    }
+    a.src[i] = static_cast<const char*>(src[i]);
+    acc += bytes[i] >> 4;
+    a.vend[i] = acc;
+  }
+  if (acc == 0) return GSEC_OK;
+  if (!dst || !aligned16(dst)) {
+    set_error("gather: destination must be 16-byte aligned");
+    return GSEC_EINVAL;
+  }
+  const int threads = 256;
+  gather_vec<<<grid_cap((acc + 3) / 4, threads), threads, 0, s>>>(a);
+  return check_launch("gather_vec");
+}
+
 unsigned layout_device_status(bool clear) {
   unsigned v = 0;
   if (cudaMemcpyFromSymbol(&v, g_layout_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;

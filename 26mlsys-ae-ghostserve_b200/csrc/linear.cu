@@ -12,6 +12,10 @@
 // replicated R times and lane l reads copy l % R: with R = 32 the 32 lanes of a
 // warp always hit 32 different banks whatever the data bytes are.
 #include "linear.cuh"
+
+#ifndef GSEC_GF8_PREFETCH
+#define GSEC_GF8_PREFETCH 1
+#endif
 #include "pipe.cuh"
 
 namespace gsec {
@@ -180,22 +184,14 @@ int launch_xor(const LinearPass& a, cudaStream_t s, int ring_bytes) {
 // of an entry = output j's product) are XORed across inputs per data byte
 // position; one 4x4 byte transpose per word then yields every output word.
 // Tables: 256 u32 entries per input, replicated R times (lane l reads copy
-// l % R, so a warp's 32 lookups hit 32 different banks when R = 32). Entries
-// are 256 bytes apart and IPB = 256 / (4R) inputs share each 256-byte entry
-// row, so the lookup address of data byte b of word d is
-//   (d.byte[b] << 8) | (lane % R) * 4      -- one byte permute (prmt)
-// plus a compile-time offset per input (64 KiB block, slot in the row) that
-// the shared-memory load takes as an immediate. Built once per CTA into a
-// compact array, then fanned out with consecutive threads writing
-// consecutive words (no bank conflicts).
+// l % R); built once per CTA into a compact array, then fanned out with
+// consecutive threads writing consecutive words (no bank conflicts).
 template <int NIN>
-__global__ void __launch_bounds__(1024, 1) gf8_fixed_kernel(const LinearPass a) {
+__global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
   constexpr int R = NIN <= 6 ? 32 : 16;
   constexpr int RSH = R == 32 ? 5 : 4;
-  constexpr int IPB = 256 / (4 * R);                      // inputs per 256-byte entry row
-  constexpr int NBLK = (NIN + IPB - 1) / IPB;             // 64 KiB blocks
-  extern __shared__ __align__(128) uint32_t tab[];        // [NBLK][256 entries][IPB][R]
-  uint32_t* compact = tab + NBLK * 16384;                 // [NIN][256]
+  extern __shared__ __align__(128) uint32_t tab[];   // [NIN][256][R]
+  uint32_t* compact = tab + NIN * 256 * R;           // [NIN][256]
   for (int e = threadIdx.x; e < NIN * 256; e += blockDim.x) {
     const int i = e >> 8, x = e & 255;
     uint32_t entry = 0;
@@ -203,22 +199,44 @@ __global__ void __launch_bounds__(1024, 1) gf8_fixed_kernel(const LinearPass a) 
     compact[e] = entry;
   }
   __syncthreads();
-  for (int w = threadIdx.x; w < NIN * 256 * R; w += blockDim.x) {
-    const int e = w >> RSH;  // compact index = input * 256 + byte value
-    const int i = e >> 8, x = e & 255;
-    tab[(i / IPB) * 16384 + x * 64 + (i % IPB) * R + (w & (R - 1))] = compact[e];
-  }
+  for (int w = threadIdx.x; w < NIN * 256 * R; w += blockDim.x) tab[w] = compact[w >> RSH];
   __syncthreads();
 
-  const uint32_t lane_off = (threadIdx.x & (R - 1)) * 4u;  // byte 0 of the address; bytes 2-3 zero
+  // Byte offset of this lane's replica inside an entry; entries are R*4 bytes
+  // apart, so (data byte << log2(R*4)) | lane_off addresses a lookup with one
+  // shift and one LOP3, the table's base being an immediate per input.
+  constexpr int ESH = RSH + 2;
+  constexpr uint32_t EMASK = 0xffu << ESH;
+  const uint32_t lane_off = (threadIdx.x & (R - 1)) * 4u;
   const unsigned char* tb = reinterpret_cast<const unsigned char*>(tab);
+  const char* in_lo[NIN];
+  const char* in_hi[NIN];
+#pragma unroll
+  for (int i = 0; i < NIN; ++i) {
+    in_lo[i] = a.in_lo[i];
+    in_hi[i] = a.in_hi[i];
+  }
   const int64_t nvec = (a.end - a.begin) >> 4;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
+#if GSEC_GF8_PREFETCH
+  // The CTA's vectors of the round GSEC_GF8_PREFETCH rounds ahead are pulled
+  // into L2 by one bulk prefetch per input, so a round's loads wait on L2
+  // rather than DRAM latency.
+  int64_t pf = (int64_t)blockIdx.x * blockDim.x + (int64_t)GSEC_GF8_PREFETCH * step;
+#endif
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
     const int64_t off = a.begin + (v << 4);
+#if GSEC_GF8_PREFETCH
+    if (threadIdx.x < NIN && a.prefetch && pf < nvec) {
+      const int64_t n = nvec - pf < (int64_t)blockDim.x ? nvec - pf : (int64_t)blockDim.x;
+      pipe::bulk_prefetch_split(in_lo[threadIdx.x], in_hi[threadIdx.x], a.split, a.begin + (pf << 4),
+                                (uint32_t)(n << 4));
+    }
+    pf += step;
+#endif
     uint4 x[NIN];
 #pragma unroll
-    for (int i = 0; i < NIN; ++i) x[i] = ld16(seg(a.in_lo[i], a.in_hi[i], a.split, off));
+    for (int i = 0; i < NIN; ++i) x[i] = ld16(seg(in_lo[i], in_hi[i], a.split, off));
     uint32_t acc[4][4];  // [word][byte position]
 #pragma unroll
     for (int w = 0; w < 4; ++w)
@@ -226,16 +244,15 @@ __global__ void __launch_bounds__(1024, 1) gf8_fixed_kernel(const LinearPass a) 
       for (int b = 0; b < 4; ++b) acc[w][b] = 0u;
 #pragma unroll
     for (int i = 0; i < NIN; ++i) {
-      const unsigned char* t = tb + (i / IPB) * 65536 + (i % IPB) * R * 4;
+      const unsigned char* t = tb + i * 256 * R * 4;
       const uint32_t xs[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         const uint32_t d = xs[w];
-        // selector: byte 0 <- lane_off byte 0, byte 1 <- d byte b, bytes 2-3 <- zero (lane_off byte 1)
-        acc[w][0] ^= *reinterpret_cast<const uint32_t*>(t + __byte_perm(d, lane_off, 0x5504));
-        acc[w][1] ^= *reinterpret_cast<const uint32_t*>(t + __byte_perm(d, lane_off, 0x5514));
-        acc[w][2] ^= *reinterpret_cast<const uint32_t*>(t + __byte_perm(d, lane_off, 0x5524));
-        acc[w][3] ^= *reinterpret_cast<const uint32_t*>(t + __byte_perm(d, lane_off, 0x5534));
+        acc[w][0] ^= *reinterpret_cast<const uint32_t*>(t + (((d << ESH) & EMASK) | lane_off));
+        acc[w][1] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (8 - ESH)) & EMASK) | lane_off));
+        acc[w][2] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (16 - ESH)) & EMASK) | lane_off));
+        acc[w][3] ^= *reinterpret_cast<const uint32_t*>(t + (((d >> (24 - ESH)) & EMASK) | lane_off));
       }
     }
     uint32_t o[4][4];  // [output][word]
@@ -459,8 +476,7 @@ int launch_gf16(const LinearPass& a, cudaStream_t s) {
 template <int NIN>
 int launch_gf8_fixed(const LinearPass& a, cudaStream_t s) {
   constexpr int R = NIN <= 6 ? 32 : 16;
-  constexpr int IPB = 256 / (4 * R);
-  const size_t smem = (size_t)((NIN + IPB - 1) / IPB) * 65536 + (size_t)NIN * 256 * 4;
+  const size_t smem = (size_t)NIN * 256 * 4 * (R + 1);
   auto k = gf8_fixed_kernel<NIN>;
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);

@@ -30,6 +30,7 @@ struct LinearPass {
   int nin;
   int nout;
   Field field;
+  int prefetch = 0;   // every input is in this GPU's memory: L2 prefetch allowed
 };
 
 // Device status word of the staged linear kernels (non-zero: a bounded wait gave up).

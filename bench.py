@@ -122,17 +122,37 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def kv_shards(torch, wl, seed: int, count: int, device):
-    """Seeded synthetic KV shards on the device (bf16 N(0,1) or fp8 uniform bytes)."""
-    gen = torch.Generator(device=device).manual_seed(seed)
-    out = []
-    for _ in range(count):
-        if wl["kv"] == "bf16":
-            x = torch.randn(wl["shard"] // 2, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
-            out.append(x.view(torch.uint8))
-        else:
-            out.append(torch.randint(0, 256, (wl["shard"],), generator=gen, device=device, dtype=torch.uint8))
-    return out
+# Inputs of the headline workloads: the known-answer cases of
+# tests/golden/kat_codes.json (the same seeded generator as tests/golden/kat.py,
+# restated here so that nothing under tests/ is imported), so the parity of the
+# timed encode is checked against the committed SHA-256 digests.
+KAT_FILE = os.path.join(ROOT, "tests", "golden", "kat_codes.json")
+KAT_CASE = {"xor_7": "config0_xor_7", "rdp_p7": "config1_rdp_p7", "rs8_6_2": "config2_rs8_6_2"}
+
+
+def kat_shard(kind: str, seed: int, j: int, nbytes: int):
+    """Data shard j of a known-answer case: bf16 bit patterns of float32
+    N(0,1) draws, or uniform bytes, from numpy's generator seeded [seed, j]."""
+    import numpy as np
+
+    rng = np.random.default_rng([seed, j])
+    if kind == "bf16":
+        x = rng.standard_normal(nbytes // 2, dtype=np.float32)
+        return (x.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+    return rng.integers(0, 256, nbytes, dtype=np.uint8)
+
+
+def kat_case(workload: str):
+    """(case record, list of host data shards) of the workload's known-answer case."""
+    with open(KAT_FILE) as f:
+        rec = json.load(f)["cases"][KAT_CASE[workload]]
+    return rec, [kat_shard(rec["kind"], rec["seed"], j, rec["shard_bytes"]) for j in range(rec["k"])]
+
+
+def sha256_dev(t) -> str:
+    import hashlib
+
+    return hashlib.sha256(t.cpu().numpy().tobytes()).hexdigest()
 
 
 # --------------------------------------------------------------- reference ----
@@ -175,34 +195,21 @@ def cpu_encode_rate(wl, host_data, seconds: float, max_reps=None):
     return alg * reps / el / 1e9, reps, threads, el
 
 
-def sample_host_data(wl, frac: float = 1.0):
-    import numpy as np
-
-    rng = np.random.default_rng(1)
-    n = wl["shard"]
-    if frac < 1.0:
-        g = (wl["p"] - 1) * wl["unit"] if wl["scheme"] == "rdp" else 4096
-        n = max(g, int(n * frac) // g * g)
-    if wl["kv"] == "bf16":
-        out = []
-        for _ in range(wl["k"]):
-            x = rng.standard_normal(n // 2, dtype=np.float32)
-            out.append((x.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8))
-        return out
-    return [rng.integers(0, 256, n, dtype=np.uint8) for _ in range(wl["k"])]
-
-
 def run_reference(args, wl):
+    """The reference arm: the CPU encoder of the same codeword on the host
+    cores, rank 0 only, each step a bounded sample of the workload."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    data = sample_host_data(wl)
+    rec, data = kat_case(args.workload)
     _, _, threads, t1 = cpu_encode_rate(wl, data, 0.0, max_reps=1)
     # each step: a bounded sample of the workload so the whole run stays within ~2 minutes
     budget = 90.0
     frac = min(1.0, budget / max(1e-9, (args.steps + args.warmup) * t1))
     if frac < 1.0:
-        data = sample_host_data(wl, frac)
+        g = (wl["p"] - 1) * wl["unit"] if wl["scheme"] == "rdp" else 4096
+        n = max(g, int(wl["shard"] * frac) // g * g)
+        data = [d[:n] for d in data]
     nbytes = data[0].size
     for _ in range(args.warmup):
         cpu_encode_rate(wl, data, 0.0, max_reps=1)
@@ -214,9 +221,9 @@ def run_reference(args, wl):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": args.workload, "desc": wl["desc"]},
         "cpu_baseline": {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "impl": CPU_IMPL[wl["scheme"]], "sample": sample},
         "e2e": {"value": round(rate, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference has no CPU encoder; this is the C/OpenMP port of the same code (oracle/cpu)",
+        "note": CPU_IMPL[wl["scheme"]] + " (oracle/cpu), on every host thread",
     }
     print(json.dumps(line), flush=True)
 
@@ -225,10 +232,11 @@ def run_reference(args, wl):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="rdp_p7", choices=sorted(WORKLOADS) + ["prefill", "hook", "sweep"])
+    ap.add_argument("--workload", default="rdp_p7",
+                    choices=sorted(WORKLOADS) + ["prefill", "hook", "sweep", "refcompat"])
     ap.add_argument("--sweep-tokens", default="256,2048,8192", help="sweep workload: chunk sizes in tokens")
     ap.add_argument("--hook-tokens", type=int, default=2048, help="hook workload: tokens per extend call")
     ap.add_argument("--hook-modes", default="fused,reference", help="hook workload: modes to time")
@@ -236,13 +244,15 @@ def main():
     ap.add_argument("--prefill-len", type=int, default=32768)
     ap.add_argument("--prefill-chunk", type=int, default=2048)
     ap.add_argument("--prefill-layers", type=int, default=32)
-    ap.add_argument("--parity", default="none,fused,reference",
-                    help="prefill variants to time: none, fused (gsec P2P encode per chunk), reference (the "
+    ap.add_argument("--parity", default="none,fused,hook,reference",
+                    help="prefill variants to time: none, fused (one P2P encode per chunk over all layers), hook "
+                         "(the drop-in hook on every layer's forward_extend, as SGLang calls it), reference (the "
                          "reference hook's gather + parity + host copy per layer)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--verify", action="store_true", help="check every rank's parity against a local re-encode")
+    ap.add_argument("--no-verify", action="store_true",
+                    help="skip the bit-exact check of the timed step's output (on by default)")
     ap.add_argument("--op", default="encode", choices=["encode", "decode"],
                     help="decode: rebuild data shards 0 and 1 (2 erasures) each step instead of encoding")
     args = ap.parse_args()
@@ -255,12 +265,16 @@ def main():
     if args.workload == "sweep":
         run_sweep(args)
         return
+    if args.workload == "refcompat":
+        run_refcompat(args)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, wl)
         return
 
     import importlib
+    import math
 
     import torch
     import torch.distributed as dist
@@ -281,24 +295,30 @@ def main():
     pbytes = spec.parity_bytes(nbytes)
     alg_bytes = k * nbytes + m * pbytes
 
-    # My data buffer holds k shard slots; slot j is shard j of codeword (rank - j) mod world.
-    slots = kv_shards(torch, wl, seed=100 + rank, count=k, device=device)
+    # Slot j of every rank holds data shard j of the known-answer codeword; rank c's
+    # codeword takes shard j from GPU (c + j) mod N, so every rank encodes the same
+    # bytes (its shards spread over the GPUs) and every parity must match the digest.
+    rec, host_data = kat_case(args.workload)
+    assert rec["shard_bytes"] == nbytes and rec["k"] == k
+    slots = [torch.from_numpy(h).to(device) for h in host_data]
     parity = [torch.empty(pbytes, dtype=torch.uint8, device=device) for _ in range(m)]
     peer_group = None
-    remote_bytes = 0
+    remote = []  # (owner rank, shard index) of the shards read over NVLink
     if world > 1:
         p2p = importlib.import_module(PKG + ".p2p")
         peer_group = p2p.PeerGroup.create(slots)  # maps every rank's k slots
         data_ptrs = [peer_group.ptr((rank + j) % world, j) for j in range(k)]
-        remote_bytes = sum(nbytes for j in range(k) if (rank + j) % world != rank)
+        remote = [((rank + j) % world, j) for j in range(k) if (rank + j) % world != rank]
     else:
         data_ptrs = [t.data_ptr() for t in slots]
+    remote_bytes = nbytes * len(remote)
     par_ptrs = [t.data_ptr() for t in parity]
     stream = torch.cuda.current_stream()
     cap = torch.cuda.Stream()  # the step is bound to this stream and replayed from a CUDA graph
     sh = int(cap.cuda_stream)
 
     step = g.codec.PreparedEncode(spec, data_ptrs, None, nbytes, nbytes, par_ptrs, 0, pbytes, sh)
+    erased, rebuilt = [], []
     if args.op == "decode":
         step()  # the parity the decode reads
         torch.cuda.synchronize()
@@ -315,18 +335,27 @@ def main():
             dist.all_reduce(t)  # stream-ordered: peers' buffers are written before anyone reads them
             torch.cuda.synchronize()
 
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # The steps run as replays of one CUDA graph of G steps, G dividing both the
+    # warm-up and the timed step counts: the W warm-up steps are W/G replays of
+    # the same graph (its first replay uploads it), the K timed steps K/G replays.
+    gcd = math.gcd(args.steps, args.warmup)
+    G = max(d for d in range(1, min(100, gcd) + 1) if gcd % d == 0)
     barrier()
     cap.wait_stream(stream)
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    # G steps per graph (the largest divisor of the step count up to 100), replayed
-    # steps / G times: exactly the requested steps, without host launch gaps
-    G = max(d for d in range(1, min(100, args.steps) + 1) if args.steps % d == 0)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=cap):
         for _ in range(G):
             step()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup // G):
+        graph.replay()
     torch.cuda.synchronize()
     barrier()
     sampler = ClockSampler(local).start()
@@ -337,28 +366,22 @@ def main():
         graph.replay()
     ev1.record(stream)
     torch.cuda.synchronize()
-    del graph
     clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
     barrier()
-    verified = None
-    if args.verify and args.op == "decode":
-        torch.cuda.synchronize()
-        ok = all(torch.equal(t, slots[e]) for e, t in zip(erased, rebuilt)) if world == 1 else True
-        verified = ok and g.codec.device_status(clear=True) == 0
-    elif args.verify:
-        verified = verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device)
-        if world > 1:
-            t = torch.tensor([0 if verified else 1], device=device)
-            dist.all_reduce(t)
-            verified = int(t.item()) == 0
+    del graph
     ms_step = ms / args.steps
     per_gpu = alg_bytes / (ms_step * 1e-3) / 1e9
     value = per_gpu * world
+
+    verified = None
+    if not args.no_verify:
+        if args.op == "decode":
+            ok = all(sha256_dev(t) == hashlib_np(host_data[e]) for e, t in zip(erased, rebuilt))
+        else:
+            ok = [sha256_dev(t) for t in parity] == rec["parity_sha256"]
+        ok = ok and g.codec.device_status(clear=True) == 0
+        verified = max_over_ranks(0.0 if ok else 1.0) == 0.0
 
     peak, peak_kind = load_peaks()
     tag = {"rdp": "rdp_encode_p7_config1", "rs8": "rs8_encode_6_2_config2", "xor": "xor_encode_7_config0"}[wl["scheme"]]
@@ -372,11 +395,12 @@ def main():
                            {"rdp": "rdp_decode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
                            )[wl["scheme"]]}
     if world > 1:
-        link = 770.0
-        t_roof = max((alg_bytes - remote_bytes) / (peak * 1e9), remote_bytes / (link * 1e9))
-        roofline["nvlink"] = {"remote_bytes_per_launch": remote_bytes, "peak_gbs_per_direction": link,
-                              "achieved_gbs": round(remote_bytes / (ms_step * 1e-3) / 1e9, 1),
-                              "roof_ms": round(t_roof * 1e3, 4), "frac_of_roof": round(t_roof * 1e3 / ms_step, 4)}
+        if args.op == "decode":  # the decode reads the survivors only
+            remote = [(o, j) for o, j in remote if j not in erased]
+            remote_bytes = nbytes * len(remote)
+        ceiling = measure_peer_read(torch, g, peer_group, remote, nbytes, device, cap, max_over_ranks, barrier)
+        roofline["nvlink"] = nvlink_roofline(alg_bytes, remote_bytes, ms_step, peak, ceiling)
+        roofline["bound"] = "nvlink" if remote_bytes / 900e9 > (alg_bytes - remote_bytes) / (peak * 1e9) else "hbm"
 
     e2e = None
     if not args.no_e2e and world == 1 and args.op == "encode":
@@ -384,9 +408,9 @@ def main():
 
     cpu_baseline = None
     if not args.no_cpu_baseline and rank == 0 and world == 1 and args.op == "encode":
-        host = [t.cpu().numpy() for t in slots]
-        rate, reps, threads, el = cpu_encode_rate(wl, host, args.cpu_seconds)
+        rate, reps, threads, el = cpu_encode_rate(wl, host_data, args.cpu_seconds)
         cpu_baseline = {"value": round(rate, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                        "impl": CPU_IMPL[wl["scheme"]],
                         "sample": f"the full workload ({k} x {nbytes} B shards) encoded {reps} times in {el:.1f} s"}
 
     if rank == 0:
@@ -397,14 +421,19 @@ def main():
             "config": {"workload": args.workload, "op": args.op, "desc": wl["desc"], "k": k, "m": m, "p": wl["p"],
                        "unit": wl["unit"], "shard_bytes": nbytes, "parity_bytes": pbytes,
                        "per_gpu_gbs": round(per_gpu, 2),
+                       "inputs": f"known-answer case {rec and KAT_CASE[args.workload]} (seeded numpy, "
+                                 f"tests/golden/kat_codes.json)",
                        "l2": f"working set {(alg_bytes) / MIB:.0f} MiB per step > 126 MB L2, no flush",
                        "placement": "single GPU" if world == 1 else "shard j of rank c's codeword on GPU (c+j)%N"},
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
-            "gpu_launches": args.steps, "launch": f"CUDA graph of {G} steps replayed {args.steps // G} times",
+            "gpu_launches": args.steps,
+            "launch": f"CUDA graph of {G} steps: {args.warmup // G} warm-up replays, {args.steps // G} timed replays",
             "clocks": clocks,
+            "verified": verified,
+            "verify": None if verified is None else (
+                "rebuilt shards' SHA-256 = the data shards'" if args.op == "decode" else
+                "parity SHA-256 = the committed known-answer digest (tests/golden/kat_codes.json), every rank"),
         }
-        if verified is not None:
-            line["verified"] = verified
         print(json.dumps(line), flush=True)
     if peer_group is not None:
         peer_group.close()
@@ -412,17 +441,233 @@ def main():
         dist.destroy_process_group()
 
 
-def verify_parity(torch, g, spec, data_ptrs, nbytes, parity, device):
-    """Copy this rank's codeword shards (local or peer) into local buffers, encode
-    them again and compare with the parity the timed loop produced."""
+CPU_IMPL = {
+    "rdp": "own C/OpenMP encoder of textbook RDP (no reference encoder exists for this code, CPU or GPU)",
+    "rs8": "own C/OpenMP encoder of RS(k,m) over GF(2^8) (no reference encoder exists for this code, CPU or GPU)",
+    "xor": "C/OpenMP port of the reference's XOR encode (benchmark/xor/kernel.cu:17-41); the reference's "
+           "own XOR is CUDA-only",
+}
+
+
+def hashlib_np(a) -> str:
+    import hashlib
+
+    return hashlib.sha256(a.tobytes()).hexdigest()
+
+
+def measure_peer_read(torch, g, peer_group, remote, nbytes, device, stream, max_over_ranks, barrier):
+    """GB/s per direction of a plain copy kernel (gsec_copy_gather, 16-byte
+    loads) that reads this rank's remote shards (the same bytes the encode
+    reads over NVLink) into local memory, all ranks at once, max over ranks."""
+    if not remote:
+        return None
     L = g._lib
-    local = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in data_ptrs]
-    for dst, src in zip(local, data_ptrs):  # gsec_rows_pack as a copy kernel (reads peer memory)
-        L.call("gsec_rows_pack", L.C.c_void_p(src), nbytes, None, 0, L.C.c_void_p(dst.data_ptr()), nbytes, nbytes, 1,
-               L.C.c_void_p(g.codec.stream_handle()))
-    again = g.encode(spec, local)
+    dst = torch.empty(nbytes * len(remote), dtype=torch.uint8, device=device)
+    srcs = L.ptr_array([peer_group.ptr(o, j) for o, j in remote])
+    sizes = (L.C.c_int64 * len(remote))(*([nbytes] * len(remote)))
+    sh = L.C.c_void_p(int(stream.cuda_stream))
+
+    def copy():
+        L.call("gsec_copy_gather", srcs, sizes, len(remote), L.C.c_void_p(dst.data_ptr()), sh)
+
+    for _ in range(3):
+        copy()
     torch.cuda.synchronize()
-    return all(torch.equal(a, b) for a, b in zip(again, parity)) and g.codec.device_status(clear=True) == 0
+    barrier()
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        copy()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+    barrier()
+    return {"gbs": round(nbytes * len(remote) / (ms * 1e-3) / 1e9, 1), "kernel": "gather_vec (gsec_copy_gather)",
+            "bytes": nbytes * len(remote), "reps": reps}
+
+
+def nvlink_roofline(alg_bytes, remote_bytes, ms_step, hbm_peak, ceiling):
+    """Roof time = max(local HBM bytes / measured HBM peak, peer bytes / link
+    bandwidth) for the 900 GB/s per-direction NVLink-5 figure and for the peer
+    read ceiling measured in the same run."""
+    def frac(link):
+        roof = max((alg_bytes - remote_bytes) / (hbm_peak * 1e9), remote_bytes / (link * 1e9))
+        return round(roof * 1e3 / ms_step, 4)
+
+    out = {"remote_bytes_per_launch": remote_bytes,
+           "achieved_gbs": round(remote_bytes / (ms_step * 1e-3) / 1e9, 1),
+           "spec_gbs_per_direction": 900.0, "frac_of_spec_roof": frac(900.0)}
+    if ceiling is not None:
+        out["measured_peer_read"] = ceiling
+        out["frac_of_measured_roof"] = frac(ceiling["gbs"])
+    return out
+
+
+# ------------------------------------------------------------- refcompat ----
+def refcompat_calls(impl: str, T: int, n: int):
+    """The reference's extension calls and Python-entry-point call sequences on
+    one rank's KV (K and V fp16 [T tokens, n = layers x heads x dim], seeded),
+    as name -> (call, output). impl "ours": this package's drop-ins
+    (``ext`` names, ``benchmark/*/main.py``); impl "reference": the reference's
+    own CUDA extensions built from its sources into oracle/_ref, called as its
+    benchmark/{xor,rdp,rs}/main.py and bench_ghostserve_rdp.py call them. Both
+    arms get the same bytes; a call's output digest must agree across arms."""
+    import importlib
+
+    import torch
+
+    gen = torch.Generator(device="cuda").manual_seed(0)
+
+    def rnd16(*shape):
+        return torch.randint(0, 1 << 16, shape, generator=gen, device="cuda", dtype=torch.int32).to(
+            torch.int16).view(torch.float16)
+
+    kt, vt = rnd16(T, n), rnd16(T, n)  # token-major K/V words
+    B, H, D = 1, n // 128, 128
+    keys, values = rnd16(B, H, T, D), rnd16(B, H, T, D)
+    world, hook_elems = 8, T * n // 8
+    hook_rows = torch.randint(0, 1 << 16, (world + 2, 2 * hook_elems), generator=gen, device="cuda",
+                              dtype=torch.int32).to(torch.int16).view(torch.uint16)
+    calls = {}
+    if impl == "reference":
+        from oracle import build_ref  # the reference arm: its own extensions only
+
+        def ext(name):
+            return build_ref.load_ref(name) if build_ref.built(name) else None
+        xk, rk, sk, hk = (ext("xor_kernel"), ext("rdp_kernel_rdp_parallel"), ext("rs_kernel16"),
+                          ext("rdp_kv_ops"))
+        if None in (xk, rk, sk, hk):
+            return None
+    else:
+        e = importlib.import_module(PKG + ".ext")
+        xk, rk, sk, hk = e.xor_kernel, e.rdp_kernel, e.rs_kernel, e.rdp_kv_ops
+    xm = importlib.import_module(PKG + ".benchmark.xor.main")
+    rm = importlib.import_module(PKG + ".benchmark.rdp.main")
+    sm = importlib.import_module(PKG + ".benchmark.rs.main")
+
+    kv_bytes = 4 * T * n
+    k = 7
+    s = -(-kv_bytes // k)
+    dp = torch.zeros(k * s, dtype=torch.uint8, device="cuda")
+    dp[:kv_bytes] = torch.cat([kt.reshape(-1), vt.reshape(-1)]).view(torch.uint8)
+    xsh = torch.zeros((k + 1, s), dtype=torch.uint8, device="cuda")
+    calls["xor_kernel.encode_xor"] = (lambda: xk.encode_xor(dp, xsh, k, s), lambda: xsh)
+
+    nd = 6
+    S = -(-(2 * T * n) // nd)
+    rsh = torch.zeros((nd + 2, S), dtype=torch.uint16, device="cuda")
+    calls["rdp_kernel.fused_backup_full_kv"] = (lambda: rk.fused_backup_full_kv(kt, vt, rsh, nd, S, T, n, 0),
+                                                lambda: rsh)
+    rout = torch.empty(2 * T * n, dtype=torch.float16, device="cuda")
+    calls["rdp_kernel.fused_recovery_full_kv (1 row lost)"] = (
+        lambda: rk.fused_recovery_full_kv(rsh, rout, nd, S, T, n, 0, 2, -1), lambda: rout)
+
+    ex, lg = sm.init_gf_tables()
+    gexp, glog = torch.from_numpy(ex).cuda(), torch.from_numpy(lg).cuda()
+    km, mm = 6, 2
+    tot = 2 * T * n
+    s16 = -(-tot // km)
+    dp16 = torch.zeros(km * s16, dtype=torch.uint16, device="cuda")
+    dp16[:tot] = torch.cat([kt.reshape(-1), vt.reshape(-1)]).view(torch.uint16)
+    ssh = torch.zeros((km + mm, s16), dtype=torch.uint16, device="cuda")
+    calls["rs_kernel.encode_rs_u16"] = (lambda: sk.encode_rs_u16(dp16, ssh, km, mm, s16, gexp, glog), lambda: ssh)
+
+    calls["rdp_kv_ops.compute_rdp_parity (world 8)"] = (
+        lambda: hk.compute_rdp_parity(hook_rows, nd=world, S=2 * hook_elems, star_base=0), lambda: hook_rows)
+
+    if impl == "reference":
+        def xor_flow():  # benchmark/xor/main.py:47-113
+            kv = torch.empty(4 * T * n, dtype=torch.uint8, device="cuda")
+            xk.pack_kv(keys, values, kv, n, T)
+            ss, _ = xm.determine_shard_size(kv.numel(), 7)
+            d = torch.zeros(7 * ss, dtype=torch.uint8, device="cuda")
+            d[:kv.numel()] = kv
+            sh = torch.zeros((8, ss), dtype=torch.uint8, device="cuda")
+            xk.encode_xor(d, sh, 7, ss)
+            return sh
+
+        def rdp_flow():  # benchmark/rdp/main.py:44-92, with its synchronisations around the kernel
+            ktn = keys.permute(2, 0, 1, 3).contiguous().view(T, n)
+            vtn = values.permute(2, 0, 1, 3).contiguous().view(T, n)
+            SS, _ = rm.determine_shard_size_words(2 * T * n, nd)
+            sh = torch.zeros((nd + 2, SS), dtype=torch.uint16, device="cuda")
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            t0.record()
+            rk.fused_backup_full_kv(ktn, vtn, sh, nd, SS, T, n, 0)
+            t1.record()
+            torch.cuda.synchronize()
+            return sh
+
+        def rs_flow():  # benchmark/rs/main.py:57-137 (GF tables built once, not per call)
+            t2 = keys.numel() + values.numel()
+            kv = torch.empty(t2, dtype=torch.uint16, device="cuda")
+            sk.pack_fp16_pair_to_u16(keys.contiguous().view(-1), values.contiguous().view(-1), kv)
+            ss, pad = sm.shard_size_and_pad(t2, km)
+            d = torch.empty(km * ss, dtype=torch.uint16, device="cuda")
+            if pad:
+                d.fill_(0)
+            d[:t2].copy_(kv)
+            sh = torch.empty((km + mm, ss), dtype=torch.uint16, device="cuda")
+            sk.encode_rs_u16(d, sh, km, mm, ss, gexp, glog)
+            return sh
+    else:
+        def xor_flow():
+            return xm.forward_encode_kv(keys, values, 7, 1)["shards_KV"]
+
+        def rdp_flow():
+            return rm.fused_backup_full_kv(keys, values, nd)["shards_KV"]
+
+        def rs_flow():
+            return sm.forward_encode_kv(keys, values, km, mm)[0]
+    box = {}
+    for name, fn in (("xor/main.py forward_encode_kv", xor_flow), ("rdp/main.py fused_backup_full_kv", rdp_flow),
+                     ("rs/main.py forward_encode_kv", rs_flow)):
+        calls[name] = ((lambda fn=fn, name=name: box.__setitem__(name, fn())), (lambda name=name: box[name]))
+    return calls
+
+
+def run_refcompat(args):
+    """The reference-layout calls of one rank's KV at two sizes (8 MiB: one
+    layer call of config 3; 32 MiB: a rank's 2048-token chunk): per-call time
+    (CUDA events on the current stream around `reps` back-to-back calls, host
+    issue included, as the reference's own demos time them) and the SHA-256 of
+    each call's output. --impl reference runs the reference's CUDA extensions,
+    the default arm this package's drop-ins; equal digests = bit-exact."""
+    import hashlib
+
+    import torch
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    out = {}
+    for label, (T, n) in (("8MiB", (1024, 2048)), ("32MiB", (2048, 4096))):
+        calls = refcompat_calls(args.impl, T, n)
+        if calls is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference extensions not built in oracle/_ref"}))
+            return
+        rows = {}
+        for name, (fn, res) in calls.items():
+            for _ in range(max(3, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            fn()
+            torch.cuda.synchronize()
+            digest = hashlib.sha256(res().contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest()[:16]
+            rows[name] = {"us": round(e0.elapsed_time(e1) / args.steps * 1e3, 2), "sha256": digest}
+        out[label] = rows
+    line = {"metric": "reference-layout call time (us per call)", "impl": args.impl, "unit": "us",
+            "higher_is_better": False, "steps": args.steps, "warmup": args.warmup,
+            "data": "synthetic (seeded random fp16 words)", "config": {"workload": "refcompat"}, "calls": out}
+    print(json.dumps(line), flush=True)
 
 
 def init_nccl():

@@ -154,6 +154,15 @@ GSEC_API int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_
                        int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n,
                        int64_t pool_rows, const void* src, gsec_stream_t stream);
 
+/* One-kernel gather: dst = src[0][0..bytes[0]) ++ ... ++ src[n-1][0..bytes[n-1])
+ * (n <= 32; every source, size and dst 16-byte aligned/multiple of 16). Sources
+ * may be mapped peer buffers: this is a plain peer-read copy (16-byte loads),
+ * the copy the reference hook does with two NCCL gathers to one rank
+ * (bench_ghostserve_rdp.py:303-332) done as reads by the destination GPU;
+ * bench.py times it as the NVLink read ceiling of a shard placement. */
+GSEC_API int gsec_copy_gather(const void* const* src, const int64_t* bytes, int32_t n, void* dst,
+                              gsec_stream_t stream);
+
 /* Stream-ordered copy of `bytes` bytes between any two addresses the device
  * can reach (device, pinned host, mapped peer). The hook offloads each parity
  * slice with it, one call per parity shard. No reference counterpart (the

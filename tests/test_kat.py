@@ -5,7 +5,7 @@ The reference has no code for textbook RDP (config 1) or RS(k,m) over GF(2^8)
 restatement of the published algorithms (``tests/golden/kat.py``: bitwise field
 arithmetic, brute-force inverses, a diagonal walk), and that restatement's
 SHA-256 digests committed in ``tests/golden/kat_codes.json`` (which the GPU
-tests and ``bench.py --verify`` compare the CUDA output against).
+tests and ``bench.py``'s default check compare the CUDA output against).
 """
 from __future__ import annotations
 
@@ -151,3 +151,25 @@ def test_fixture_lists_every_case():
         rec = f[case[0]]
         assert (rec["scheme"], rec["k"], rec["m"], rec["p"], rec["unit"], rec["kind"], rec["shard_bytes"],
                 rec["seed"]) == tuple(case[1:])
+
+
+def test_bench_inputs_are_the_known_answer_cases():
+    """bench.py restates the seeded generator (it imports nothing from tests/):
+    the restatement must give the same bytes, and its workloads the sizes of
+    the committed cases, so its parity check against the digests is valid."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    for kind in ("bf16", "u8"):
+        for j in (0, 3):
+            assert np.array_equal(bench.kat_shard(kind, 77, j, 4096), kat.shard_bytes(kind, 77, j, 4096))
+    f = fixture()["cases"]
+    for wl, case in bench.KAT_CASE.items():
+        w, rec = bench.WORKLOADS[wl], f[case]
+        assert (w["scheme"], w["k"], w["m"], w["p"], w["shard"]) == (rec["scheme"], rec["k"], rec["m"], rec["p"],
+                                                                      rec["shard_bytes"])
+        if w["scheme"] == "rdp":
+            assert w["unit"] == rec["unit"]
+        assert rec["kind"] == ("bf16" if w["kv"] == "bf16" else "u8")
