@@ -261,24 +261,6 @@ int gsec_parity_bytes(const gsec_code* code, int64_t data_bytes, int64_t* out) {
   return GSEC_OK;
 }
 
-namespace {
-// True when every input of the pass is device memory (this GPU's or a mapped
-// peer's), which the GF(2^8) kernel may ask the L2 to prefetch; pinned host
-// inputs read through unified addressing are left alone.
-bool inputs_on_device(const LinearPass& a) {
-  for (int i = 0; i < a.nin; ++i)
-    for (const char* p : {a.in_lo[i], a.in_hi[i]}) {
-      cudaPointerAttributes attr{};
-      if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-      }
-      if (attr.type != cudaMemoryTypeDevice) return false;
-    }
-  return true;
-}
-}  // namespace
-
 int gsec_encode(const gsec_code* code, const void* const* data_lo, const void* const* data_hi, int64_t split,
                 int64_t data_bytes, void* const* parity, int64_t begin, int64_t end, gsec_stream_t stream) {
   int rc = check_code(code);
@@ -335,7 +317,6 @@ int gsec_encode(const gsec_code* code, const void* const* data_lo, const void* c
     a.out_end[j] = end;
     for (int i = 0; i < k; ++i) a.coef[j][i] = rs8_gen(k, k + j, i);
   }
-  if (a.field == Field::GF8) a.prefetch = inputs_on_device(a) ? 1 : 0;
   return run_linear(a, s);
 }
 
@@ -454,7 +435,6 @@ int gsec_decode(const gsec_code* code, void* const* shard_lo, void* const* shard
     a.out_hi[e] = hi(row);
     a.out_end[e] = row < k ? data_bytes : end;
   }
-  a.prefetch = inputs_on_device(a) ? 1 : 0;
   return run_linear(a, s);
 }
 

@@ -12,10 +12,6 @@
 // replicated R times and lane l reads copy l % R: with R = 32 the 32 lanes of a
 // warp always hit 32 different banks whatever the data bytes are.
 #include "linear.cuh"
-
-#ifndef GSEC_GF8_PREFETCH
-#define GSEC_GF8_PREFETCH 1
-#endif
 #include "pipe.cuh"
 
 namespace gsec {
@@ -218,22 +214,8 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
   }
   const int64_t nvec = (a.end - a.begin) >> 4;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
-#if GSEC_GF8_PREFETCH
-  // The CTA's vectors of the round GSEC_GF8_PREFETCH rounds ahead are pulled
-  // into L2 by one bulk prefetch per input, so a round's loads wait on L2
-  // rather than DRAM latency.
-  int64_t pf = (int64_t)blockIdx.x * blockDim.x + (int64_t)GSEC_GF8_PREFETCH * step;
-#endif
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
     const int64_t off = a.begin + (v << 4);
-#if GSEC_GF8_PREFETCH
-    if (threadIdx.x < NIN && a.prefetch && pf < nvec) {
-      const int64_t n = nvec - pf < (int64_t)blockDim.x ? nvec - pf : (int64_t)blockDim.x;
-      pipe::bulk_prefetch_split(in_lo[threadIdx.x], in_hi[threadIdx.x], a.split, a.begin + (pf << 4),
-                                (uint32_t)(n << 4));
-    }
-    pf += step;
-#endif
     uint4 x[NIN];
 #pragma unroll
     for (int i = 0; i < NIN; ++i) x[i] = ld16(seg(in_lo[i], in_hi[i], a.split, off));

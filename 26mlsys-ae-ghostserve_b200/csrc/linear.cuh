@@ -30,7 +30,7 @@ struct LinearPass {
   int nin;
   int nout;
   Field field;
-  int prefetch = 0;   // every input is in this GPU's memory: L2 prefetch allowed
+  uint32_t unity = 1;  // always 1; read from the launch parameters, so the compiler cannot fold it
 };
 
 // Device status word of the staged linear kernels (non-zero: a bounded wait gave up).

@@ -79,25 +79,6 @@ __device__ __forceinline__ void bulk_load_split(void* dst, const char* lo, const
   }
 }
 
-// Ask the L2 to fetch bytes [src, src + bytes) (multiple of 16, 16-byte
-// aligned) ahead of their use; nothing waits for it and no data moves to the SM.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-// bulk_prefetch_l2 of bytes [off, off + bytes) of the two-segment string lo ++ hi.
-__device__ __forceinline__ void bulk_prefetch_split(const char* lo, const char* hi, int64_t split, int64_t off,
-                                                    uint32_t bytes) {
-  if (off + bytes <= split) {
-    bulk_prefetch_l2(lo + off, bytes);
-  } else if (off >= split) {
-    bulk_prefetch_l2(hi + (off - split), bytes);
-  } else {
-    const uint32_t b0 = (uint32_t)(split - off);
-    bulk_prefetch_l2(lo + off, b0);
-    bulk_prefetch_l2(hi, bytes - b0);
-  }
-}
-
 // Consumer side: every lane of the warp has finished reading the stage; one
 // arrival per warp (the empty barrier counts warps).
 __device__ __forceinline__ void warp_release(uint64_t* b) {
