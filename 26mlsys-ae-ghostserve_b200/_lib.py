@@ -69,6 +69,10 @@ _SIGS = {
     "gsec_copy_gather": (C.c_int, [_PP, C.POINTER(_I64), _I32, _P, _P]),
     "gsec_slots_gather": (C.c_int, [_P, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P]),
     "gsec_slots_scatter": (C.c_int, [_P, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P]),
+    "gsec_slots_gather_pools": (C.c_int, [_PP, _I32, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P, _I64,
+                                          _P]),
+    "gsec_slots_scatter_pools": (C.c_int, [_PP, _I32, _I64, _I64, _I32, _I64, _P, _I32, _I64, _I64, _P, _P, _I64,
+                                           _P]),
     "gsec_xor_encode": (C.c_int, [_P, _P, _I32, _I64, _I64, _P]),
     "gsec_xor_reconstruct": (C.c_int, [_P, _P, _I64, _I64, _I32, _PI32, _I32, _P]),
     "gsec_rdpref_pack_row": (C.c_int, [_P, _P, _I64, _P, _I64, _I32, _P]),

@@ -462,25 +462,52 @@ bool slot_geometry_ok(int64_t pitch, int64_t plane, int32_t nplanes, int64_t row
 int gsec_slots_gather(const void* pool, int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes,
                       const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows, void* dst,
                       gsec_stream_t stream) {
-  GSEC_REQUIRE(pool != nullptr && dst != nullptr && (n == 0 || slots != nullptr), "null pointer");
-  GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
-  GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
-  GSEC_REQUIRE(slot_geometry_ok(pitch, plane, nplanes, row_bytes),
-               "slot record: need pitch > 0, plane >= 0 and (nplanes-1)*plane + row_bytes <= pitch");
-  return slots_move(true, const_cast<void*>(pool), pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
-                    dst, as_stream(stream));
+  void* pools[1] = {const_cast<void*>(pool)};
+  return gsec_slots_gather_pools(pools, 1, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows, dst,
+                                 nullptr, INT64_MAX, stream);
 }
 
 int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_t nplanes, int64_t row_bytes,
                        const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows, const void* src,
                        gsec_stream_t stream) {
-  GSEC_REQUIRE(pool != nullptr && src != nullptr && (n == 0 || slots != nullptr), "null pointer");
+  void* pools[1] = {pool};
+  return gsec_slots_scatter_pools(pools, 1, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                                  src, nullptr, INT64_MAX, stream);
+}
+
+namespace {
+int slots_args_ok(const void* const* pools, int32_t npools, int64_t pitch, int64_t plane, int32_t nplanes,
+                  int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows,
+                  const void* lo) {
+  GSEC_REQUIRE(pools != nullptr && lo != nullptr && (n == 0 || slots != nullptr), "null pointer");
+  GSEC_REQUIRE(npools >= 1, "npools=%d must be >= 1", npools);
+  for (int q = 0; q < npools; ++q) GSEC_REQUIRE(pools[q] != nullptr, "null pointer (pool %d)", q);
   GSEC_REQUIRE(slot_bytes == 4 || slot_bytes == 8, "slot_bytes=%d must be 4 or 8", slot_bytes);
   GSEC_REQUIRE(nplanes >= 1 && n >= 0 && pool_rows >= 0, "bad nplanes/n/pool_rows");
   GSEC_REQUIRE(slot_geometry_ok(pitch, plane, nplanes, row_bytes),
                "slot record: need pitch > 0, plane >= 0 and (nplanes-1)*plane + row_bytes <= pitch");
-  return slots_move(false, pool, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
-                    const_cast<void*>(src), as_stream(stream));
+  return GSEC_OK;
+}
+}  // namespace
+
+int gsec_slots_gather_pools(void* const* pools, int32_t npools, int64_t pitch, int64_t plane, int32_t nplanes,
+                            int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows,
+                            void* dst_lo, void* dst_hi, int64_t split, gsec_stream_t stream) {
+  const int rc = slots_args_ok(pools, npools, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                               dst_lo);
+  if (rc) return rc;
+  return slots_move(true, pools, npools, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows, dst_lo,
+                    dst_hi, split, as_stream(stream));
+}
+
+int gsec_slots_scatter_pools(void* const* pools, int32_t npools, int64_t pitch, int64_t plane, int32_t nplanes,
+                             int64_t row_bytes, const void* slots, int32_t slot_bytes, int64_t n, int64_t pool_rows,
+                             const void* src_lo, const void* src_hi, int64_t split, gsec_stream_t stream) {
+  const int rc = slots_args_ok(pools, npools, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                               src_lo);
+  if (rc) return rc;
+  return slots_move(false, pools, npools, pitch, plane, nplanes, row_bytes, slots, slot_bytes, n, pool_rows,
+                    const_cast<void*>(src_lo), const_cast<void*>(src_hi), split, as_stream(stream));
 }
 
 int gsec_copy_gather(const void* const* src, const int64_t* bytes, int32_t n, void* dst, gsec_stream_t stream) {

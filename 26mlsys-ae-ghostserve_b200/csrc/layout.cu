@@ -398,52 +398,58 @@ int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t
 }
 
 // ------------------------------------------------- pool rows by slot index --
-// The KV pool of an attention backend is [slots, planes, ...] (for SGLang's
-// FlashInfer pool: planes K and V). One extend call's delta KV is the rows of
-// its slot list; the reference copies them out with two fancy-index gathers,
-// after a device-to-host read of the active count (bench_ghostserve_rdp.py:
-// 449-458). slots_gather writes plane p's rows, in slot-list order, to
-// dst[p*n*row_bytes ...] in one pass (a slot < 0 gives a zero row, so no count
-// is needed on the host); slots_scatter writes such a buffer back into the pool
-// (rows of slots < 0 are skipped). A slot >= pool_rows is an error: the row is
-// zeroed (gather) or skipped (scatter) and bit 0 of the layout status is set.
+// The KV pool of an attention backend is [slots, planes, ...] per layer (for
+// SGLang's FlashInfer pool: planes K and V). One extend call's delta KV is the
+// rows of its slot list; the reference copies them out with two fancy-index
+// gathers, after a device-to-host read of the active count
+// (bench_ghostserve_rdp.py:449-458). slots_gather writes, for every pool q (a
+// layer) and plane p, the rows of the slot list in list order to the byte
+// stream position ((q * nplanes + p) * n + i) * row_bytes of a two-segment
+// destination (lo[0..split) ++ hi[...]), one launch for every layer of a
+// chunk; a slot < 0 gives a zero row, so no count is needed on the host.
+// slots_scatter writes such a stream back into the pools (rows of slots < 0
+// are skipped). A slot >= pool_rows is an error: the row is zeroed (gather) or
+// skipped (scatter) and bit 0 of the layout status is set.
 static __device__ unsigned g_layout_status;
 
 namespace {
-template <typename I>
-__global__ void slots_gather_vec(const char* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
-                                 const I* slots, int64_t n, int64_t pool_rows, char* dst) {
-  const int64_t vpr = row_bytes >> 4;
-  const int64_t total = vpr * n * nplanes;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pr = v / vpr;  // plane * n + list position
-    const int64_t x = (v - pr * vpr) << 4;
-    const int64_t p = pr / n, i = pr - p * n;
-    const int64_t slot = (int64_t)slots[i];
-    uint4 val = vzero();
-    if (slot >= pool_rows) {
-      if (x == 0) atomicOr(&g_layout_status, 1u);
-    } else if (slot >= 0) {
-      val = ldv(pool + slot * pitch + p * plane + x);
-    }
-    stv(dst + pr * row_bytes + x, val);
-  }
+constexpr int kMaxPools = 128;
+struct SlotArgs {
+  char* pool[kMaxPools];
+  int npools;
+  int nplanes;
+  int64_t pitch, plane, row_bytes, n, pool_rows, split;
+  char* lo;
+  char* hi;
+};
+
+__device__ __forceinline__ char* seg_at(const SlotArgs& a, int64_t o) {
+  return o < a.split ? a.lo + o : a.hi + (o - a.split);
 }
 
-template <typename I>
-__global__ void slots_scatter_vec(char* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
-                                  const I* slots, int64_t n, int64_t pool_rows, const char* src) {
-  const int64_t vpr = row_bytes >> 4;
-  const int64_t total = vpr * n * nplanes;
+template <typename I, bool GATHER>
+__global__ void slots_vec(const SlotArgs a, const I* slots) {
+  const int64_t vpr = a.row_bytes >> 4;
+  const int64_t rows = a.n * a.nplanes * a.npools;
+  const int64_t total = vpr * rows;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pr = v / vpr;
-    const int64_t x = (v - pr * vpr) << 4;
-    const int64_t p = pr / n, i = pr - p * n;
+    const int64_t r = v / vpr;  // (pool * nplanes + plane) * n + list position
+    const int64_t x = (v - r * vpr) << 4;
+    const int64_t qp = r / a.n, i = r - qp * a.n;
+    const int64_t q = qp / a.nplanes, p = qp - q * a.nplanes;
     const int64_t slot = (int64_t)slots[i];
-    if (slot >= pool_rows) {
+    char* stream = seg_at(a, r * a.row_bytes + x);
+    if (slot >= a.pool_rows) {
       if (x == 0) atomicOr(&g_layout_status, 1u);
+      if (GATHER) stv(stream, vzero());
     } else if (slot >= 0) {
-      stv(pool + slot * pitch + p * plane + x, ldv(src + pr * row_bytes + x));
+      char* row = a.pool[q] + slot * a.pitch + p * a.plane + x;
+      if (GATHER)
+        stv(stream, ldv(row));
+      else
+        stv(row, ldv(stream));
+    } else if (GATHER) {
+      stv(stream, vzero());
     }
   }
 }
@@ -522,35 +528,53 @@ unsigned layout_device_status(bool clear) {
   return v;
 }
 
-int slots_move(bool gather, void* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
-               const void* slots, int slot_bytes, int64_t n, int64_t pool_rows, void* buf, cudaStream_t s) {
+int slots_move(bool gather, void* const* pools, int npools, int64_t pitch, int64_t plane, int nplanes,
+               int64_t row_bytes, const void* slots, int slot_bytes, int64_t n, int64_t pool_rows, void* lo,
+               void* hi, int64_t split, cudaStream_t s) {
   if (n == 0) return GSEC_OK;
-  if (!aligned16(pool) || !aligned16(buf) || (pitch & 15) || (plane & 15) || (row_bytes & 15) || row_bytes <= 0) {
-    set_error("slot rows: pool, buffer, pitch, plane offset and row bytes must be 16-byte aligned");
+  if (npools < 1 || npools > kMaxPools) {
+    set_error("slot rows: 1..%d pools", kMaxPools);
     return GSEC_EINVAL;
   }
+  const int64_t total = (int64_t)npools * nplanes * n * row_bytes;
+  const bool two = hi != nullptr && split < total;
+  if (!aligned16(lo) || (two && (!aligned16(hi) || (split & 15) || split < 0)) || (pitch & 15) || (plane & 15) ||
+      (row_bytes & 15) || row_bytes <= 0) {
+    set_error("slot rows: pools, buffer, split, pitch, plane offset and row bytes must be 16-byte aligned");
+    return GSEC_EINVAL;
+  }
+  SlotArgs a{};
+  for (int q = 0; q < npools; ++q) {
+    if (!pools[q] || !aligned16(pools[q])) {
+      set_error("slot rows: pool %d is null or not 16-byte aligned", q);
+      return GSEC_EINVAL;
+    }
+    a.pool[q] = static_cast<char*>(pools[q]);
+  }
+  a.npools = npools;
+  a.nplanes = nplanes;
+  a.pitch = pitch;
+  a.plane = plane;
+  a.row_bytes = row_bytes;
+  a.n = n;
+  a.pool_rows = pool_rows;
+  a.lo = static_cast<char*>(lo);
+  a.hi = two ? static_cast<char*>(hi) : a.lo;
+  a.split = two ? split : INT64_MAX;
   const int threads = 256;
-  const int grid = grid_cap((row_bytes >> 4) * n * nplanes, threads);
+  const int grid = grid_cap((row_bytes >> 4) * n * nplanes * npools, threads);
   if (gather) {
     if (slot_bytes == 8)
-      slots_gather_vec<<<grid, threads, 0, s>>>(static_cast<const char*>(pool), pitch, plane, nplanes, row_bytes,
-                                                static_cast<const int64_t*>(slots), n, pool_rows,
-                                                static_cast<char*>(buf));
+      slots_vec<int64_t, true><<<grid, threads, 0, s>>>(a, static_cast<const int64_t*>(slots));
     else
-      slots_gather_vec<<<grid, threads, 0, s>>>(static_cast<const char*>(pool), pitch, plane, nplanes, row_bytes,
-                                                static_cast<const int32_t*>(slots), n, pool_rows,
-                                                static_cast<char*>(buf));
-    return check_launch("slots_gather_vec");
+      slots_vec<int32_t, true><<<grid, threads, 0, s>>>(a, static_cast<const int32_t*>(slots));
+    return check_launch("slots_gather");
   }
   if (slot_bytes == 8)
-    slots_scatter_vec<<<grid, threads, 0, s>>>(static_cast<char*>(pool), pitch, plane, nplanes, row_bytes,
-                                               static_cast<const int64_t*>(slots), n, pool_rows,
-                                               static_cast<const char*>(buf));
+    slots_vec<int64_t, false><<<grid, threads, 0, s>>>(a, static_cast<const int64_t*>(slots));
   else
-    slots_scatter_vec<<<grid, threads, 0, s>>>(static_cast<char*>(pool), pitch, plane, nplanes, row_bytes,
-                                               static_cast<const int32_t*>(slots), n, pool_rows,
-                                               static_cast<const char*>(buf));
-  return check_launch("slots_scatter_vec");
+    slots_vec<int32_t, false><<<grid, threads, 0, s>>>(a, static_cast<const int32_t*>(slots));
+  return check_launch("slots_scatter");
 }
 
 }  // namespace gsec

@@ -16,8 +16,9 @@ int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t
                 int64_t H, int64_t T, int64_t D, cudaStream_t s);
 
 // Pool rows by slot index (gather: pool -> buf, scatter: buf -> pool); see layout.cu.
-int slots_move(bool gather, void* pool, int64_t pitch, int64_t plane, int nplanes, int64_t row_bytes,
-               const void* slots, int slot_bytes, int64_t n, int64_t pool_rows, void* buf, cudaStream_t s);
+int slots_move(bool gather, void* const* pools, int npools, int64_t pitch, int64_t plane, int nplanes,
+               int64_t row_bytes, const void* slots, int slot_bytes, int64_t n, int64_t pool_rows, void* lo,
+               void* hi, int64_t split, cudaStream_t s);
 // Status word of the slot kernels (bit 0: a slot past the pool's rows).
 int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, cudaStream_t s);
 unsigned layout_device_status(bool clear);

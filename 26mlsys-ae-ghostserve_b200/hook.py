@@ -61,6 +61,10 @@ class HookConfig:
     prog_start_mono: float = field(default_factory=lambda: float(os.getenv("FT_PROG_START_MONO", "nan")))
     compat_cast_fp16: bool = True       # reference mode: .to(float16) as bench_ghostserve_rdp.py:345-346
     broadcast_chunk_id: bool = True     # reference mode: rank-0 counter + broadcast (:287-301)
+    protect: str = "call"               # fused mode: "call" encodes after every forward_extend call (as the
+                                        # reference does); "chunk" encodes once per prefill chunk, after the
+                                        # chunk_layers-th call, all layers' delta KV in one codeword
+    chunk_layers: int = field(default_factory=lambda: int(os.getenv("FT_CHUNK_LAYERS", "0")))
     offload: bool = True                # copy parity to pinned host memory
     host_keep: int = 256                # chunks whose parity slice stays in pinned host memory
     host_budget: int = 1 << 30          # bytes of the pinned ring holding them (at least 4 chunks' worth)
@@ -90,6 +94,7 @@ class KVFaultTolerance:
         self._plans = {}          # (slot, half, stream) -> marshalled encode of that staging slot
         self._pools = {}          # KV pool geometry by (pointer, shape, strides)
         self._events = []         # timing events free for reuse
+        self._chunk_pools = []    # protect="chunk": this chunk's pools seen so far (one per layer call)
 
     # ------------------------------------------------------------- control --
     def _rank_world(self):
@@ -240,15 +245,18 @@ class KVFaultTolerance:
                              lambda slot: self._stage(slot, half, parts_k, parts_v),
                              lambda slot: self._unstage(slot, parts_k, parts_v))
 
-    def recover_pool(self, chunk_id: int, lost, kv_pool: torch.Tensor, slots: torch.Tensor):
-        """recover_parts for a chunk encoded by encode_pool: survivors gather the
-        slot list's rows again, the lost ranks' rebuilt rows are scattered back
-        into their pool at the same slots (rows of negative slots untouched)."""
-        geo = self._pool_geometry(kv_pool)
-        half = slots.numel() * geo[0]
-        self._recover_staged(chunk_id, lost, half, kv_pool.device,
-                             lambda slot: self._gather_pool(kv_pool, geo, slots, slot, True),
-                             lambda slot: self._gather_pool(kv_pool, geo, slots, slot, False))
+    def recover_pool(self, chunk_id: int, lost, kv_pool, slots: torch.Tensor):
+        """recover_parts for a chunk encoded by encode_pool (one pool) or
+        encode_pools (a list of per-layer pools, the hook's per-chunk mode):
+        survivors gather the slot list's rows again, the lost ranks' rebuilt rows
+        are scattered back into their pools at the same slots (rows of negative
+        slots untouched)."""
+        pools = list(kv_pool) if isinstance(kv_pool, (list, tuple)) else [kv_pool]
+        geo = self._pools_geometry(pools)
+        half = len(pools) * slots.numel() * geo[0]
+        self._recover_staged(chunk_id, lost, half, pools[0].device,
+                             lambda slot: self._gather_pools(pools, geo, slots, slot, True),
+                             lambda slot: self._gather_pools(pools, geo, slots, slot, False))
 
     def _recover_staged(self, chunk_id, lost, half, device, stage, unstage):
         rank, world = self._rank_world()
@@ -306,20 +314,28 @@ class KVFaultTolerance:
     def encode_pool(self, kv_pool: torch.Tensor, slots: torch.Tensor, chunk_id: int):
         """encode_chunk of one extend call's delta KV read straight out of the KV
         pool [slots, 2 (K, V), heads, head_dim] through its slot list: one
-        gather kernel per plane writes the rows into the staging buffer (a
-        negative slot is a zero row), so neither the active count nor the
+        gather kernel writes the K rows and the V rows into the staging buffer
+        (a negative slot is a zero row), so neither the active count nor the
         gathered K/V ever reaches the host (bench_ghostserve_rdp.py:449-458 reads
         the count back and copies the rows twice). Every rank of the group must
         pass a slot list of the same length (tensor-parallel ranks share it)."""
-        device = kv_pool.device
-        geo = self._pool_geometry(kv_pool)
-        half = slots.numel() * geo[0]
+        return self.encode_pools([kv_pool], slots, chunk_id)
+
+    def encode_pools(self, pools, slots: torch.Tensor, chunk_id: int):
+        """encode_pool over several pools that share one slot list (the
+        per-layer pools of one prefill chunk): one gather launch stages every
+        layer's K and V rows ([pool 0 K, pool 0 V, pool 1 K, ...]), then one
+        barrier, one sliced encode and one host copy protect the whole chunk."""
+        pools = list(pools)
+        device = pools[0].device
+        geo = self._pools_geometry(pools)
+        half = len(pools) * slots.numel() * geo[0]
         if half % 16:
             raise ValueError("pool rows must be multiples of 16 bytes")
         self._ensure_staging(half, device)
         slot = self._calls % 2
         self._calls += 1
-        self._gather_pool(kv_pool, geo, slots, slot, True)
+        self._gather_pools(pools, geo, slots, slot, True)
         return self._encode_staged(slot, half, chunk_id, device)
 
     def _pool_geometry(self, kv_pool):
@@ -332,18 +348,32 @@ class KVFaultTolerance:
             geo = self._pools[key] = (row, pitch, voff)
         return geo
 
-    def _gather_pool(self, kv_pool, geo, slots, slot, gather: bool):
-        """K and V planes of the slot list's rows into (gather) or out of
-        (scatter) staging slot `slot`: two gsec_slots_* calls."""
+    def _pools_geometry(self, pools):
+        """The common geometry of a list of pools (every pool checked, cached)."""
+        geo = self._pool_geometry(pools[0])
+        rows = pools[0].shape[0]
+        for p in pools[1:]:
+            if self._pool_geometry(p) != geo or p.shape[0] != rows or p.device != pools[0].device:
+                raise ValueError("the pools of one chunk must share shape, strides, dtype and device")
+        return geo
+
+    def _gather_pools(self, pools, geo, slots, slot, gather: bool):
+        """K and V planes of the slot list's rows in every pool into (gather) or
+        out of (scatter) staging slot `slot`: one gsec_slots_*_pools call; the
+        row stream [pool 0 K, pool 0 V, pool 1 K, ...] runs through the K
+        buffer and on into the V buffer."""
         if slots.dtype not in (torch.int32, torch.int64) or not slots.is_contiguous() or \
-                slots.device != kv_pool.device:
+                slots.device != pools[0].device:
             raise ValueError("slots must be a contiguous int32/int64 tensor on the pool's device")
         row, pitch, voff = geo
-        fn = _lib.lib().gsec_slots_gather if gather else _lib.lib().gsec_slots_scatter
-        base, sp, n, es = kv_pool.data_ptr(), slots.data_ptr(), slots.numel(), slots.element_size()
-        stream = torch.cuda.current_stream(kv_pool.device).cuda_stream
-        for plane_off, buf in ((0, self._staging[slot][0]), (voff, self._staging[slot][1])):
-            _lib.check(fn(base + plane_off, pitch, 0, 1, row, sp, es, n, kv_pool.shape[0], buf.data_ptr(), stream))
+        fn = _lib.lib().gsec_slots_gather_pools if gather else _lib.lib().gsec_slots_scatter_pools
+        n = slots.numel()
+        half = len(pools) * n * row
+        stream = torch.cuda.current_stream(pools[0].device).cuda_stream
+        ptrs = _lib.ptr_array([p.data_ptr() for p in pools])
+        _lib.check(fn(ptrs, len(pools), pitch, voff, 2, row, slots.data_ptr(), slots.element_size(), n,
+                      pools[0].shape[0], self._staging[slot][0].data_ptr(), self._staging[slot][1].data_ptr(), half,
+                      stream))
 
     def _parity_bufs(self, nbytes: int, m: int, device):
         """The two device parity slots (m buffers each) with room for nbytes."""
@@ -513,10 +543,21 @@ class KVFaultTolerance:
             # the pool is read through the slot list on the device: no host sync
             if slots.numel() == 0:
                 return
+            if self.cfg.protect == "chunk":
+                # one codeword per prefill chunk: remember this layer's pool and
+                # encode after the chunk's last layer call
+                if self.cfg.chunk_layers < 1:
+                    raise ValueError("protect='chunk' needs chunk_layers (the model's layer count)")
+                self._chunk_pools.append(kv_pool)
+                if len(self._chunk_pools) < self.cfg.chunk_layers:
+                    return
+                pools, self._chunk_pools = self._chunk_pools, []
+            else:
+                pools = [kv_pool]
             chunk_id, _ = self.next_chunk_id(device=kv_pool.device)
             if self.first_chunk_wall_ms is None and self.cfg.prog_start_mono == self.cfg.prog_start_mono:
                 self.first_chunk_wall_ms = (time.perf_counter() - self.cfg.prog_start_mono) * 1000.0
-            self.encode_pool(kv_pool, slots.contiguous(), chunk_id)
+            self.encode_pools(pools, slots.contiguous(), chunk_id)
             return
         active = slots != -1
         if int(active.sum().item()) == 0:

@@ -10,20 +10,30 @@ random bf16 weights) split Megatron-style over the ranks of a process group:
 
 * QKV and gate/up projections column-parallel, O and down projections
   row-parallel followed by an all-reduce (NCCL);
-* every rank owns kv_heads / world KV heads in a layer-major cache
-  ``[layers, kv_heads_rank, max_tokens, 128]`` for K and for V;
+* every rank owns kv_heads / world KV heads of the KV cache (layouts below);
 * a chunk of T tokens at position p attends to the cache prefix [0, p + T) with
   lower-right causal masking (scaled_dot_product_attention, grouped-query).
 
-Parity hooks:
-* ``parity="fused"``: after all layers of a chunk, the chunk's K and V of every
-  layer on this rank form its data shard; ``KVFaultTolerance.encode_parts``
-  stages them and encodes this rank's slice of the world-wide code with NVLink
-  peer reads, parity to pinned host memory asynchronously;
-* ``parity="reference"``: the reference hook's flow after every layer's
-  attention (chunk id broadcast, gather to the rotating destination, fp16 cast,
-  mod-S parity, synchronous copy to the host), as the reference runs it
-  (bench_ghostserve_rdp.py:424-471, once per forward_extend call).
+KV cache layout: SGLang's FlashInfer pool, one pool per layer of
+``[max_tokens, 2 (K, V), kv_heads_rank, 128]`` (``layout="pool"``, the
+default; slot = token position), or a layer-major ``[layers, kv_heads_rank,
+max_tokens, 128]`` pair (``layout="layer"``).
+
+Parity variants (``run_prefill``):
+* ``"hook"``: the drop-in hook as SGLang drives it — a FlashInfer-named
+  attention backend patched with ``hook.patch_backend``; after every layer's
+  attention its ``forward_extend`` is called with the chunk's slot mapping and
+  that layer's pool, so the hook (``protect="call"``) encodes every layer's
+  delta KV separately, 32 times per chunk, like the reference hook
+  (bench_ghostserve_rdp.py:424-476);
+* ``"hook_chunk"``: the same calls with ``protect="chunk"``: the hook keeps the
+  layers' pools and encodes once per chunk, after the last layer's call (one
+  gather launch over all layers, one barrier, one sliced encode, one host copy);
+* ``"fused"``: after all layers of a chunk, ``KVFaultTolerance.encode_parts``
+  on the chunk's K and V views of every layer (staged by copies);
+* ``"reference"``: the reference hook's flow after every layer's attention
+  (chunk id broadcast, gather to the rotating destination, fp16 cast, mod-S
+  parity, synchronous copy to the host), once per forward_extend call.
 """
 from __future__ import annotations
 
@@ -52,7 +62,7 @@ class ModelSpec:
 class TPPrefill:
     """One rank's slice of the model and its KV cache."""
 
-    def __init__(self, spec: ModelSpec, max_tokens: int, device, group=None, seed: int = 0):
+    def __init__(self, spec: ModelSpec, max_tokens: int, device, group=None, seed: int = 0, layout: str = "pool"):
         self.spec = spec
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -76,8 +86,14 @@ class TPPrefill:
                 ln1=torch.ones(H, device=self.device, dtype=torch.bfloat16),
                 ln2=torch.ones(H, device=self.device, dtype=torch.bfloat16)))
         self.embed = rnd(spec.vocab, H, std=1.0)
-        self.kcache = torch.empty(spec.layers, self.hk, max_tokens, D, device=self.device, dtype=torch.bfloat16)
-        self.vcache = torch.empty_like(self.kcache)
+        if layout not in ("pool", "layer"):
+            raise ValueError("layout must be 'pool' or 'layer'")
+        self.layout = layout
+        if layout == "pool":  # per layer [slots, 2, kv_heads, D]: slot s holds token s's K and V
+            self.pool = torch.empty(spec.layers, max_tokens, 2, self.hk, D, device=self.device, dtype=torch.bfloat16)
+        else:
+            self.kcache = torch.empty(spec.layers, self.hk, max_tokens, D, device=self.device, dtype=torch.bfloat16)
+            self.vcache = torch.empty_like(self.kcache)
         inv = 1.0 / (spec.rope_theta ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float32) / D))
         ang = torch.outer(torch.arange(max_tokens, device=self.device, dtype=torch.float32), inv)
         self.cos, self.sin = ang.cos(), ang.sin()
@@ -115,13 +131,19 @@ class TPPrefill:
             q = self._rope(qkv[:, :hq * D].view(T, hq, D), pos0)
             k = self._rope(qkv[:, hq * D:(hq + hk) * D].view(T, hk, D), pos0)
             v = qkv[:, (hq + hk) * D:].view(T, hk, D)
-            self.kcache[li, :, pos0:pos0 + T] = k.transpose(0, 1)
-            self.vcache[li, :, pos0:pos0 + T] = v.transpose(0, 1)
-            o = F.scaled_dot_product_attention(
-                q.transpose(0, 1)[None], self.kcache[li, :, :pos0 + T][None], self.vcache[li, :, :pos0 + T][None],
-                attn_mask=mask, enable_gqa=hq != hk)
+            if self.layout == "pool":
+                self.pool[li, pos0:pos0 + T, 0] = k
+                self.pool[li, pos0:pos0 + T, 1] = v
+                kc = self.pool[li, :pos0 + T, 0].transpose(0, 1)
+                vc = self.pool[li, :pos0 + T, 1].transpose(0, 1)
+            else:
+                self.kcache[li, :, pos0:pos0 + T] = k.transpose(0, 1)
+                self.vcache[li, :, pos0:pos0 + T] = v.transpose(0, 1)
+                kc, vc = self.kcache[li, :, :pos0 + T], self.vcache[li, :, :pos0 + T]
+            o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], kc[None], vc[None], attn_mask=mask,
+                                               enable_gqa=hq != hk)
             if after_attention is not None:
-                after_attention(li, self.kcache[li, :, pos0:pos0 + T], self.vcache[li, :, pos0:pos0 + T])
+                after_attention(li, kc[:, pos0:pos0 + T], vc[:, pos0:pos0 + T])
             o = o[0].transpose(0, 1).reshape(T, hq * D) @ L["wo"]
             x = x + self._all_reduce(o)
             h = self._norm(x, L["ln2"])
@@ -132,13 +154,41 @@ class TPPrefill:
 
     def chunk_kv_parts(self, pos0: int, T: int):
         """The chunk's K and V of every layer on this rank (views into the cache)."""
+        if self.layout == "pool":
+            return ([self.pool[li, pos0:pos0 + T, 0] for li in range(self.spec.layers)],
+                    [self.pool[li, pos0:pos0 + T, 1] for li in range(self.spec.layers)])
         return ([self.kcache[li, :, pos0:pos0 + T] for li in range(self.spec.layers)],
                 [self.vcache[li, :, pos0:pos0 + T] for li in range(self.spec.layers)])
 
+    def layer_pool(self, li: int) -> torch.Tensor:
+        """Layer li's KV pool [slots, 2, kv_heads_rank, head_dim] (layout "pool")."""
+        return self.pool[li]
 
-def run_prefill(model: TPPrefill, seqs: int, seq_len: int, chunk: int, parity: str, ft=None, seed: int = 1) -> int:
+
+class FlashInferAttnBackend:
+    """The attention-backend object the hook patches (it only needs the class
+    name, ``forward_extend`` and the pool attribute). ``kv_buffer`` is set to
+    the pool of the layer whose extend call is being made."""
+
+    def __init__(self):
+        self.kv_buffer = None
+
+    def forward_extend(self, batch, layer=None, save_kv_cache=True):
+        return None
+
+
+class ExtendBatch:
+    """The part of SGLang's forward batch the hook reads: the chunk's slot mapping."""
+
+    def __init__(self, slot_mapping: torch.Tensor):
+        self.slot_mapping = slot_mapping
+
+
+def run_prefill(model: TPPrefill, seqs: int, seq_len: int, chunk: int, parity: str, ft=None, seed: int = 1,
+                backend: Optional[FlashInferAttnBackend] = None) -> int:
     """Prefill `seqs` sequences of `seq_len` random token ids chunk by chunk;
-    returns the number of tokens processed."""
+    returns the number of tokens processed. parity "hook"/"hook_chunk" need
+    `backend`, a FlashInferAttnBackend patched with hook.patch_backend(backend, ft)."""
     gen = torch.Generator(device=model.device).manual_seed(seed)
     cid = 0
     for _ in range(seqs):
@@ -152,6 +202,12 @@ def run_prefill(model: TPPrefill, seqs: int, seq_len: int, chunk: int, parity: s
                     got = ft.gather_kv(k.transpose(0, 1), v.transpose(0, 1), dst)
                     if got is not None:
                         ft.compute_parity_to_cpu(*got, chunk_id, dst)
+            elif parity in ("hook", "hook_chunk"):
+                batch = ExtendBatch(torch.arange(pos0, pos0 + T, device=model.device, dtype=torch.int64))
+
+                def cb(li, k, v, batch=batch):  # SGLang's extend call of layer li
+                    backend.kv_buffer = model.layer_pool(li)
+                    backend.forward_extend(batch, layer=li)
             model.forward_chunk(ids[pos0:pos0 + T], pos0, after_attention=cb)
             if parity == "fused":
                 cid += 1

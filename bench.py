@@ -244,10 +244,11 @@ def main():
     ap.add_argument("--prefill-len", type=int, default=32768)
     ap.add_argument("--prefill-chunk", type=int, default=2048)
     ap.add_argument("--prefill-layers", type=int, default=32)
-    ap.add_argument("--parity", default="none,fused,hook,reference",
-                    help="prefill variants to time: none, fused (one P2P encode per chunk over all layers), hook "
-                         "(the drop-in hook on every layer's forward_extend, as SGLang calls it), reference (the "
-                         "reference hook's gather + parity + host copy per layer)")
+    ap.add_argument("--parity", default="none,hook_chunk,hook,reference",
+                    help="prefill variants to time: none; hook (the drop-in hook on every layer's "
+                         "forward_extend, one encode per call, as SGLang drives the reference hook); hook_chunk (the "
+                         "same calls, one encode per chunk after the last layer); fused (encode_parts once per "
+                         "chunk); reference (the reference hook's gather + parity + host copy per layer call)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -948,7 +949,10 @@ def run_sweep(args):
 
 def run_prefill_bench(args):
     """Config 3: TP prefill of a Llama-3.1-8B-architecture model (random bf16
-    weights), prefill tokens/s without parity and with it (fused / reference)."""
+    weights, SGLang-style per-layer KV pools), prefill tokens/s without parity
+    and with each parity variant (prefill.run_prefill): the drop-in hook on
+    every layer's forward_extend (per call, and batched per chunk), the fused
+    per-chunk encode, and the reference hook's flow."""
     import importlib
 
     import torch
@@ -961,19 +965,23 @@ def run_prefill_bench(args):
     model = pre.TPPrefill(spec, args.prefill_len, device)
     chunk = args.prefill_chunk
     variants = [v for v in args.parity.split(",") if v]
-    rates, times = {}, {}
-    recovery = None
+    rates, times, recovery = {}, {}, {}
     for var in variants:
-        ft = None
+        ft, backend = None, None
         if var != "none":
-            ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused" if var == "fused" else "reference",
-                                                       metrics_file=None))
-        pre.run_prefill(model, 1, min(2 * chunk, args.prefill_len), chunk, var, ft, seed=7)  # warm-up
+            cfg = hook.HookConfig(mode="reference" if var == "reference" else "fused", metrics_file=None,
+                                  protect="chunk" if var == "hook_chunk" else "call",
+                                  chunk_layers=spec.layers)
+            ft = hook.KVFaultTolerance(cfg)
+            if var in ("hook", "hook_chunk"):
+                backend = pre.FlashInferAttnBackend()
+                assert hook.patch_backend(backend, ft)
+        pre.run_prefill(model, 1, min(2 * chunk, args.prefill_len), chunk, var, ft, seed=7, backend=backend)
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        tokens = pre.run_prefill(model, args.prefill_seqs, args.prefill_len, chunk, var, ft)
+        tokens = pre.run_prefill(model, args.prefill_seqs, args.prefill_len, chunk, var, ft, backend=backend)
         if ft is not None:
             ft.flush()  # the last chunk's parity has reached host memory
         e1.record()
@@ -982,38 +990,48 @@ def run_prefill_bench(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times[var] = float(t.item())
         rates[var] = tokens / (times[var] * 1e-3)
-        if var == "fused":
-            recovery = measure_recovery(torch, dist, model, ft, args, device)
+        if var in ("fused", "hook_chunk"):
+            recovery[var] = measure_recovery(torch, dist, model, ft, args, device, var)
         if ft is not None:
             ft.close()
     base = rates.get("none")
     if rank == 0:
-        head = "fused" if "fused" in rates else variants[0]
+        head = next((v for v in ("hook_chunk", "hook", "fused") if v in rates), variants[0])
         line = {
             "metric": "prefill tok/s with per-chunk KV parity (Llama-3.1-8B arch, random bf16 weights)",
             "value": round(rates[head], 1), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
             "scaling": "strong", "dtype": "bf16", "data": "synthetic (uniform random token ids)",
             "config": {"workload": "prefill", "tp": world, "seqs": args.prefill_seqs, "seq_len": args.prefill_len,
-                       "chunk": chunk, "layers": args.prefill_layers, "parity_code": "fused: RDP over the TP ranks' "
-                       "per-chunk KV (k = world), reference: mod-S RDP gathered to a rotating rank per layer"},
+                       "chunk": chunk, "layers": args.prefill_layers, "value_variant": head,
+                       "kv_cache": "per-layer pools [slots, 2, kv_heads/TP, 128] bf16 (SGLang FlashInfer layout)",
+                       "parity_code": "hook/hook_chunk/fused: RDP over the TP ranks' delta KV (k = TP), "
+                                      "reference: mod-S RDP gathered to a rotating rank per layer call",
+                       "variants": {
+                           "hook": "drop-in hook on every layer's forward_extend, one encode per call (32/chunk)",
+                           "hook_chunk": "same calls, hook protect='chunk': one encode per chunk after the "
+                                         "last layer",
+                           "fused": "KVFaultTolerance.encode_parts once per chunk (staged by copies)",
+                           "reference": "the reference hook's flow on every layer call"}},
             "tok_s": {k: round(v, 1) for k, v in rates.items()},
             "ms": {k: round(v, 2) for k, v in times.items()},
             "overhead_pct": {k: round(100.0 * (base / v - 1.0), 2) for k, v in rates.items()
                              if base and k != "none"},
         }
-        if recovery is not None:
+        if recovery:
             line["recover"] = recovery
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
 
-def measure_recovery(torch, dist, model, ft, args, device):
+def measure_recovery(torch, dist, model, ft, args, device, variant):
     """Rebuild the last sequence's chunk KV of lost rank(s) from the host parity
-    store (KVFaultTolerance.recover_parts): one lost rank (rank 1, or 0 at TP=1)
-    and, for TP >= 2, ranks 0 and 1 together. The lost ranks' chunk KV is zeroed
-    first and compared with a saved copy afterwards. Time per chunk = max over
-    ranks of CUDA-event time over the chunks still held."""
+    store: one lost rank (rank 1, or 0 at TP=1) and, for TP >= 2, ranks 0 and
+    1 together. variant "fused": recover_parts on the chunk's K/V views;
+    "hook_chunk": recover_pool on the layers' pools through the chunk's slot
+    list. The lost ranks' chunk KV is zeroed first and compared with a saved
+    copy afterwards. Time per chunk = max over ranks of CUDA-event time over
+    the chunks still held."""
     chunk, n = args.prefill_chunk, args.prefill_len
     rank, world = ft._rank_world()
     per_seq = (n + chunk - 1) // chunk
@@ -1021,6 +1039,7 @@ def measure_recovery(torch, dist, model, ft, args, device):
     # the last sequence's chunks whose parity is still in the host store
     held = [(cid, pos0) for cid, pos0 in zip(range(last - per_seq + 1, last + 1), range(0, n, chunk))
             if cid in ft._store]
+    pools = [model.layer_pool(li) for li in range(model.spec.layers)] if variant == "hook_chunk" else None
     out = {"chunks_held": len(held), "chunks_in_sequence": per_seq}
     for lost in ([1], [0, 1]) if world >= 2 else ([0],):
         saved = []
@@ -1036,8 +1055,12 @@ def measure_recovery(torch, dist, model, ft, args, device):
         e0.record()
         rebuilt = 0
         for cid, pos0 in held:
-            pk, pv = model.chunk_kv_parts(pos0, min(chunk, n - pos0))
-            ft.recover_parts(cid, lost, pk, pv)
+            T = min(chunk, n - pos0)
+            pk, pv = model.chunk_kv_parts(pos0, T)
+            if pools is not None:
+                ft.recover_pool(cid, lost, pools, torch.arange(pos0, pos0 + T, device=device, dtype=torch.int64))
+            else:
+                ft.recover_parts(cid, lost, pk, pv)
             rebuilt += len(lost) * 2 * sum(x.numel() * x.element_size() for x in pk)
         e1.record()
         torch.cuda.synchronize()

@@ -163,6 +163,25 @@ GSEC_API int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_
 GSEC_API int gsec_copy_gather(const void* const* src, const int64_t* bytes, int32_t n, void* dst,
                               gsec_stream_t stream);
 
+/* gsec_slots_gather over the same slot list in several pools at once (the
+ * per-layer KV pools of one attention backend, npools <= 128, all of the same
+ * geometry): pool q, plane p, list position i goes to byte
+ * ((q*nplanes + p)*n + i)*row_bytes of the two-segment destination
+ * dst_lo[0..split) ++ dst_hi[...] (dst_hi = NULL: one buffer). One launch
+ * gathers a prefill chunk's delta KV of every layer, which the hook's
+ * per-chunk mode encodes once instead of once per layer call; the reference
+ * has no such mode (it encodes after every forward_extend call,
+ * bench_ghostserve_rdp.py:424-471). */
+GSEC_API int gsec_slots_gather_pools(void* const* pools, int32_t npools, int64_t pitch, int64_t plane,
+                                     int32_t nplanes, int64_t row_bytes, const void* slots, int32_t slot_bytes,
+                                     int64_t n, int64_t pool_rows, void* dst_lo, void* dst_hi, int64_t split,
+                                     gsec_stream_t stream);
+/* Inverse of gsec_slots_gather_pools (rows of negative slots are skipped). */
+GSEC_API int gsec_slots_scatter_pools(void* const* pools, int32_t npools, int64_t pitch, int64_t plane,
+                                      int32_t nplanes, int64_t row_bytes, const void* slots, int32_t slot_bytes,
+                                      int64_t n, int64_t pool_rows, const void* src_lo, const void* src_hi,
+                                      int64_t split, gsec_stream_t stream);
+
 /* Stream-ordered copy of `bytes` bytes between any two addresses the device
  * can reach (device, pinned host, mapped peer). The hook offloads each parity
  * slice with it, one call per parity shard. No reference counterpart (the

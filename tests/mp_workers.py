@@ -345,3 +345,105 @@ def hook_reference(rank, world, port, backend, out):
     dist.all_gather_object(oks, (ok, len(seen)))
     out.put((rank, oks, recs))
     dist.destroy_process_group()
+
+
+def chunk_mode_calls(rank, world, port, out):
+    """protect="chunk" on the host: the hook encodes once per chunk_layers
+    extend calls, with that chunk's pools in call order (encode_pools mocked)."""
+    _init(rank, world, port)
+    hook = _pkg("hook")
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", protect="chunk", chunk_layers=3, metrics_file=None))
+    got = []
+    ft.encode_pools = lambda pools, slots, cid: got.append(([int(p[0, 0, 0, 0]) for p in pools], cid,
+                                                            slots.tolist()))
+
+    class Batch:
+        def __init__(self, sm):
+            self.slot_mapping = sm
+
+    pools = [torch.full((8, 2, 1, 8), float(li)) for li in range(3)]
+    for c in range(2):
+        sm = torch.arange(4) + 4 * c
+        for li in range(3):
+            ft.on_extend(Batch(sm), pools[li])
+    out.put((rank, got))
+    dist.destroy_process_group()
+
+
+def hook_pool_chunk(rank, world, port, backend, out):
+    """protect="chunk" on the GPU: three layers' pools (one per extend call of
+    a chunk) are encoded as one codeword per chunk whose data shard is the row
+    stream [layer 0 K, layer 0 V, layer 1 K, ...]; parity must equal the
+    oracle's, and recover_pool with the list of pools must bring a lost rank's
+    rows back bit-exact in every layer."""
+    _init(rank, world, port, backend)
+    dev = rank if backend == "nccl" else 0
+    torch.cuda.set_device(dev)
+    hook = _pkg("hook")
+    from oracle import codes
+
+    L = 3
+    g = torch.Generator(device="cuda").manual_seed(300 + rank)
+    pools = [torch.randn(256, 2, 2, 64, device="cuda", generator=g).to(torch.bfloat16) for _ in range(L)]
+
+    class FlashInferAttnBackend:
+        kv_buffer = None
+
+        def forward_extend(self, batch, layer=None, save_kv_cache=True):
+            return "attn-out"
+
+    class Batch:
+        def __init__(self, slot_mapping):
+            self.slot_mapping = slot_mapping
+
+    be = FlashInferAttnBackend()
+    ft = hook.KVFaultTolerance(hook.HookConfig(mode="fused", scheme="rdp", unit=1024, protect="chunk",
+                                               chunk_layers=L, metrics_file=None))
+    assert hook.patch_backend(be, ft)
+    gen = torch.Generator().manual_seed(6)
+    calls = []
+    for n in (64, 24):
+        perm = torch.randperm(256, generator=gen)[:n]
+        perm[torch.randperm(n, generator=gen)[: n // 8]] = -1
+        calls.append(perm.cuda())
+    ok = True
+    spec = ft._spec(world)
+    for sm in calls:
+        for li in range(L):
+            be.kv_buffer = pools[li]
+            assert be.forward_extend(Batch(sm), layer=li) == "attn-out"
+        torch.cuda.synchronize()
+        s64 = sm.to(torch.int64)
+        parts = []
+        for p in pools:
+            rows = p[s64.clamp(min=0)].clone()
+            rows[s64 < 0] = 0
+            parts += [rows[:, 0].reshape(-1).view(torch.uint8), rows[:, 1].reshape(-1).view(torch.uint8)]
+        shard = torch.cat(parts)
+        shards = [None] * world
+        dist.all_gather_object(shards, shard.cpu().numpy())
+        ft.flush()
+        entry = ft._store[ft.chunk_counter]
+        mine = entry["host"].numpy().copy()
+        got = [None] * world
+        dist.all_gather_object(got, (entry["lo"], entry["hi"], mine))
+        if rank == 0:
+            want = codes.rdp_encode(list(shards), spec.p, spec.unit)
+            for j in range(2):
+                sl = [x[2][j * (x[1] - x[0]):(j + 1) * (x[1] - x[0])] for x in got]
+                ok = ok and np.array_equal(np.concatenate(sl), want[j])
+    for lost in ([1], [0, 1]) if world > 1 else ([0],):
+        saved = [p.clone() for p in pools]
+        for cid, sm in enumerate(calls, start=1):
+            if rank in lost:
+                s64 = sm.to(torch.int64)
+                for p in pools:
+                    p[s64[s64 >= 0]] = 0
+            ft.recover_pool(cid, lost, pools, sm)
+        torch.cuda.synchronize()
+        ok = ok and all(torch.equal(p, q) for p, q in zip(pools, saved))
+    ft.close()
+    oks = [None] * world
+    dist.all_gather_object(oks, ok)
+    out.put((rank, all(oks), [r["chunk_id"] for r in ft.records]))
+    dist.destroy_process_group()

@@ -40,3 +40,10 @@ def test_hook_reads_kv_pool_through_slot_mapping():
     for _rank, ok, recs in res:
         assert ok is True
         assert recs == [1, 2, 3]
+
+
+def test_hook_chunk_mode_encodes_all_layers_once():
+    res = run_ranks(mp_workers.hook_pool_chunk, 2, "gloo", timeout=300)
+    for _rank, ok, recs in res:
+        assert ok is True
+        assert recs == [1, 2]

@@ -157,3 +157,11 @@ def test_stripe_slices_partition():
             sizes = [b - a for a, b in cuts]
             assert max(sizes) - min(sizes) <= 1
     assert p2p.codeword_placement(3, 8, 6) == [3, 4, 5, 6, 7, 0]
+
+
+def test_chunk_mode_encodes_once_per_chunk():
+    res = run_ranks(mp_workers.chunk_mode_calls, 1)
+    _rank, got = res[0]
+    assert [g[0] for g in got] == [[0, 1, 2], [0, 1, 2]]  # the chunk's pools, in layer order
+    assert [g[1] for g in got] == [1, 2]                  # one chunk id per chunk
+    assert got[1][2] == [4, 5, 6, 7]
