@@ -1035,7 +1035,9 @@ def measure_recovery(torch, dist, model, ft, args, device, variant):
     chunk, n = args.prefill_chunk, args.prefill_len
     rank, world = ft._rank_world()
     per_seq = (n + chunk - 1) // chunk
-    last = args.prefill_seqs * per_seq  # chunk id of the last chunk
+    # chunk id of the last chunk: run_prefill numbers the fused variant's chunks
+    # from 1 on every call; the hook numbers its chunks on from the warm-up's
+    last = ft.chunk_counter if variant == "hook_chunk" else args.prefill_seqs * per_seq
     # the last sequence's chunks whose parity is still in the host store
     held = [(cid, pos0) for cid, pos0 in zip(range(last - per_seq + 1, last + 1), range(0, n, chunk))
             if cid in ft._store]
