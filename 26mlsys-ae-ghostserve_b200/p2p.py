@@ -8,9 +8,9 @@ CUDA IPC handle + offset per buffer), the handles go around the process group
 buffers.  The encode kernel then reads peer shards in place with NVLink peer
 loads; no copy kernel or NCCL data call sits on that path.
 
-No multicast: peer memory is read by plain per-CTA cp.async.bulk copies
-(TMA bulk copies without .multicast::cluster) into the reading CTA's own
-shared memory, or by 16-byte loads.
+Peer memory is read by plain per-CTA cp.async.bulk copies (each CTA loads
+its own copy into its own shared memory; no cluster multicast anywhere), or by
+16-byte loads.
 """
 from __future__ import annotations
 
