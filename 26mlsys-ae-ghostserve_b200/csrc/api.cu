@@ -41,6 +41,13 @@ int check_launch(const char* what) {
   return GSEC_OK;
 }
 
+int launch_rc(cudaError_t rc, const char* what) {
+  if (rc == cudaSuccess) return check_launch(what);
+  cudaGetLastError();
+  set_error("%s: %s", what, cudaGetErrorString(rc));
+  return GSEC_ECUDA;
+}
+
 int current_device() {
   int dev = -1;
   return cudaGetDevice(&dev) == cudaSuccess ? dev : -1;

@@ -10,6 +10,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/gsec.h"
 
@@ -30,6 +31,8 @@ const char* last_error();
 
 // Returns GSEC_ECUDA with the launch error if the last launch failed.
 int check_launch(const char* what);
+// GSEC_OK, or GSEC_ECUDA with the message of `rc` (a cudaLaunchKernelEx result).
+int launch_rc(cudaError_t rc, const char* what);
 
 inline cudaStream_t as_stream(gsec_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -37,6 +40,36 @@ inline cudaStream_t as_stream(gsec_stream_t s) { return reinterpret_cast<cudaStr
 int sm_count();
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#ifndef GSEC_PDL
+#define GSEC_PDL 1
+#endif
+// Programmatic dependent launch: a kernel launched with launch_pdl may be
+// started while the previous kernel in its stream is still finishing. Its CTAs
+// set up (shared-memory barriers, tables) and then wait in grid_dep_wait()
+// until every prerequisite grid has completed and its memory operations are
+// visible, so no global memory is touched early; grid_dep_launch() lets the
+// next kernel in the stream be scheduled the same way. Back-to-back launches
+// then overlap their launch latency and ramp-up with the previous one's tail.
+// Kernels launched without the attribute pass through both instructions.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = GSEC_PDL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 #ifndef GSEC_BALANCED_GRID
 #define GSEC_BALANCED_GRID 1

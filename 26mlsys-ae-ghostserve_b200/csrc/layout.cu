@@ -32,6 +32,8 @@ int grid_cap(int64_t items, int threads) {
 // ----------------------------------------------------------- rows <-> stream
 __global__ void rows_pack_vec(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
                               int64_t pitch, int64_t row_bytes, int nrows) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t vpr = row_bytes >> 4;  // row_bytes is a multiple of 16 here
   const int64_t total = vpr * nrows;
   const int64_t stream = len0 + len1;
@@ -64,6 +66,8 @@ __device__ __forceinline__ char stream_byte(const char* s0, int64_t len0, const 
 
 __global__ void rows_pack_any(const char* s0, int64_t len0, const char* s1, int64_t len1, char* rows,
                               int64_t pitch, int64_t row_bytes, int nrows) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t slots = (row_bytes >> 4) + 2;  // head + whole vectors + tail of a row
   const int64_t total = slots * nrows;
   const int64_t stream = len0 + len1;
@@ -90,6 +94,8 @@ __global__ void rows_pack_any(const char* s0, int64_t len0, const char* s1, int6
 
 __global__ void rows_unpack_vec(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
                                 char* d1, int64_t len1) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t stream = len0 + len1;
   const int64_t total = (stream + 15) >> 4;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
@@ -115,6 +121,8 @@ __global__ void rows_unpack_vec(const char* rows, int64_t pitch, int64_t row_byt
 // vector whose 16 source bytes lie in one row is read with an ldu16 window.
 __global__ void rows_unpack_any(const char* rows, int64_t pitch, int64_t row_bytes, char* d0, int64_t len0,
                                 char* d1, int64_t len1) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t na = (len0 >> 4) + 2, nb = (len1 >> 4) + 2;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < na + nb; g += (int64_t)gridDim.x * blockDim.x) {
     const bool first = g < na;
@@ -184,6 +192,8 @@ __device__ __forceinline__ int64_t perm_d(const Perm& p, int64_t j) {
 // group of 8 stream words maps to 8 consecutive source words.
 __global__ void bhtd_pack_kernel(const uint16_t* k, const uint16_t* v, Perm p, uint16_t* rows, int64_t pitch,
                                  int64_t S, int nd, bool vec) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t groups = (S + 7) >> 3;
   const int64_t total = groups * nd;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
@@ -204,6 +214,8 @@ __global__ void bhtd_pack_kernel(const uint16_t* k, const uint16_t* v, Perm p, u
 
 __global__ void bhtd_unpack_kernel(const uint16_t* rows, int64_t pitch, int64_t S, Perm p, uint16_t* k,
                                    uint16_t* v, bool vec) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t total = (2 * p.Tn + 7) >> 3;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i0 = g << 3;
@@ -234,6 +246,8 @@ __device__ __forceinline__ uint16_t bhtd_word(const uint16_t* k, const uint16_t*
 
 __global__ void bhtd_pack_any(const uint16_t* k, const uint16_t* v, Perm p, uint16_t* rows, int64_t pitch,
                               int64_t S, int nd) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t slots = (S >> 3) + 2;
   const int64_t total = slots * nd;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
@@ -286,6 +300,8 @@ __global__ void bhtd_pack_any(const uint16_t* k, const uint16_t* v, Perm p, uint
 // consecutive stream words, read with one ldu16 window when they lie in one row.
 __global__ void bhtd_unpack_any(const uint16_t* rows, int64_t pitch, int64_t S, Perm p, uint16_t* k,
                                 uint16_t* v) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t per = (p.Tn >> 3) + 2;  // slots of one tensor
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < 2 * per; g += (int64_t)gridDim.x * blockDim.x) {
     const bool isk = g < per;
@@ -336,11 +352,17 @@ int rows_pack(const void* s0, int64_t len0, const void* s1, int64_t len1, void* 
                    (len0 == 0 || aligned16(a)) && (len1 == 0 || aligned16(b));
   const int threads = 256;
   if (vec) {
-    rows_pack_vec<<<grid_cap((row_bytes >> 4) * nrows, threads), threads, 0, s>>>(
-        a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
+    if (const cudaError_t lrc = launch_pdl(rows_pack_vec,
+                                           dim3((unsigned)(grid_cap((row_bytes >> 4) * nrows, threads))),
+                                           dim3(threads), 0, s, a, len0, b, len1, static_cast<char*>(rows), pitch,
+                                           row_bytes, nrows))
+      return launch_rc(lrc, "rows_pack_vec");
   } else {
-    rows_pack_any<<<grid_cap(((row_bytes >> 4) + 2) * nrows, threads), threads, 0, s>>>(
-        a, len0, b, len1, static_cast<char*>(rows), pitch, row_bytes, nrows);
+    if (const cudaError_t lrc = launch_pdl(rows_pack_any,
+                                           dim3((unsigned)(grid_cap(((row_bytes >> 4) + 2) * nrows, threads))),
+                                           dim3(threads), 0, s, a, len0, b, len1, static_cast<char*>(rows), pitch,
+                                           row_bytes, nrows))
+      return launch_rc(lrc, "rows_pack_any");
   }
   return check_launch("rows_pack");
 }
@@ -357,11 +379,17 @@ int rows_unpack(const void* rows, int64_t pitch, int64_t row_bytes, int nrows, v
                    (len0 == 0 || aligned16(a)) && (len1 == 0 || aligned16(b));
   const int threads = 256;
   if (vec) {
-    rows_unpack_vec<<<grid_cap((len0 + len1 + 15) >> 4, threads), threads, 0, s>>>(
-        static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
+    if (const cudaError_t lrc = launch_pdl(rows_unpack_vec,
+                                           dim3((unsigned)(grid_cap((len0 + len1 + 15) >> 4, threads))),
+                                           dim3(threads), 0, s, static_cast<const char*>(rows), pitch, row_bytes, a,
+                                           len0, b, len1))
+      return launch_rc(lrc, "rows_unpack_vec");
   } else {
-    rows_unpack_any<<<grid_cap((len0 >> 4) + (len1 >> 4) + 4, threads), threads, 0, s>>>(
-        static_cast<const char*>(rows), pitch, row_bytes, a, len0, b, len1);
+    if (const cudaError_t lrc = launch_pdl(rows_unpack_any,
+                                           dim3((unsigned)(grid_cap((len0 >> 4) + (len1 >> 4) + 4, threads))),
+                                           dim3(threads), 0, s, static_cast<const char*>(rows), pitch, row_bytes, a,
+                                           len0, b, len1))
+      return launch_rc(lrc, "rows_unpack_any");
   }
   return check_launch("rows_unpack");
 }
@@ -375,10 +403,14 @@ int bhtd_pack(const uint16_t* k, const uint16_t* v, int64_t B, int64_t H, int64_
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
   if (!vec) {
-    bhtd_pack_any<<<grid_cap(((S >> 3) + 2) * nd, threads), threads, 0, s>>>(k, v, p, rows, pitch, S, nd);
+    if (const cudaError_t lrc = launch_pdl(bhtd_pack_any, dim3((unsigned)(grid_cap(((S >> 3) + 2) * nd, threads))),
+                                           dim3(threads), 0, s, k, v, p, rows, pitch, S, nd))
+      return launch_rc(lrc, "bhtd_pack_any");
     return check_launch("bhtd_pack_any");
   }
-  bhtd_pack_kernel<<<grid_cap(((S + 7) >> 3) * nd, threads), threads, 0, s>>>(k, v, p, rows, pitch, S, nd, vec);
+  if (const cudaError_t lrc = launch_pdl(bhtd_pack_kernel, dim3((unsigned)(grid_cap(((S + 7) >> 3) * nd, threads))),
+                                         dim3(threads), 0, s, k, v, p, rows, pitch, S, nd, vec))
+    return launch_rc(lrc, "bhtd_pack_kernel");
   return check_launch("bhtd_pack_kernel");
 }
 
@@ -390,10 +422,16 @@ int bhtd_unpack(const uint16_t* rows, int64_t pitch, int nd, int64_t S, uint16_t
   const bool vec = (D % 8 == 0) && (S % 8 == 0) && (pitch % 8 == 0) && aligned16(k) && aligned16(v) && aligned16(rows);
   const int threads = 256;
   if (!vec) {
-    bhtd_unpack_any<<<grid_cap(2 * ((p.Tn >> 3) + 2), threads), threads, 0, s>>>(rows, pitch, S, p, k, v);
+    if (const cudaError_t lrc = launch_pdl(bhtd_unpack_any,
+                                           dim3((unsigned)(grid_cap(2 * ((p.Tn >> 3) + 2), threads))), dim3(threads),
+                                           0, s, rows, pitch, S, p, k, v))
+      return launch_rc(lrc, "bhtd_unpack_any");
     return check_launch("bhtd_unpack_any");
   }
-  bhtd_unpack_kernel<<<grid_cap((2 * p.Tn + 7) >> 3, threads), threads, 0, s>>>(rows, pitch, S, p, k, v, vec);
+  if (const cudaError_t lrc = launch_pdl(bhtd_unpack_kernel,
+                                         dim3((unsigned)(grid_cap((2 * p.Tn + 7) >> 3, threads))), dim3(threads), 0,
+                                         s, rows, pitch, S, p, k, v, vec))
+    return launch_rc(lrc, "bhtd_unpack_kernel");
   return check_launch("bhtd_unpack_kernel");
 }
 
@@ -429,6 +467,8 @@ __device__ __forceinline__ char* seg_at(const SlotArgs& a, int64_t o) {
 
 template <typename I, bool GATHER>
 __global__ void slots_vec(const SlotArgs a, const I* slots) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t vpr = a.row_bytes >> 4;
   const int64_t rows = a.n * a.nplanes * a.npools;
   const int64_t total = vpr * rows;
@@ -476,6 +516,8 @@ __device__ __forceinline__ const char* gather_src(const GatherArgs& a, int64_t v
 }
 
 __global__ void __launch_bounds__(256) gather_vec(const GatherArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t total = a.vend[a.n - 1];
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += 4 * step) {
@@ -514,7 +556,9 @@ int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, 
     return GSEC_EINVAL;
   }
   const int threads = 256;
-  gather_vec<<<grid_cap((acc + 3) / 4, threads), threads, 0, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(gather_vec, dim3((unsigned)(grid_cap((acc + 3) / 4, threads))),
+                                         dim3(threads), 0, s, a))
+    return launch_rc(lrc, "gather_vec");
   return check_launch("gather_vec");
 }
 
@@ -565,15 +609,23 @@ int slots_move(bool gather, void* const* pools, int npools, int64_t pitch, int64
   const int grid = grid_cap((row_bytes >> 4) * n * nplanes * npools, threads);
   if (gather) {
     if (slot_bytes == 8)
-      slots_vec<int64_t, true><<<grid, threads, 0, s>>>(a, static_cast<const int64_t*>(slots));
+      if (const cudaError_t lrc = launch_pdl(slots_vec<int64_t, true>, dim3((unsigned)(grid)), dim3(threads), 0, s,
+                                             a, static_cast<const int64_t*>(slots)))
+        return launch_rc(lrc, "slots_vec");
     else
-      slots_vec<int32_t, true><<<grid, threads, 0, s>>>(a, static_cast<const int32_t*>(slots));
+      if (const cudaError_t lrc = launch_pdl(slots_vec<int32_t, true>, dim3((unsigned)(grid)), dim3(threads), 0, s,
+                                             a, static_cast<const int32_t*>(slots)))
+        return launch_rc(lrc, "slots_vec");
     return check_launch("slots_gather");
   }
   if (slot_bytes == 8)
-    slots_vec<int64_t, false><<<grid, threads, 0, s>>>(a, static_cast<const int64_t*>(slots));
+    if (const cudaError_t lrc = launch_pdl(slots_vec<int64_t, false>, dim3((unsigned)(grid)), dim3(threads), 0, s, a,
+                                           static_cast<const int64_t*>(slots)))
+      return launch_rc(lrc, "slots_vec");
   else
-    slots_vec<int32_t, false><<<grid, threads, 0, s>>>(a, static_cast<const int32_t*>(slots));
+    if (const cudaError_t lrc = launch_pdl(slots_vec<int32_t, false>, dim3((unsigned)(grid)), dim3(threads), 0, s, a,
+                                           static_cast<const int32_t*>(slots)))
+      return launch_rc(lrc, "slots_vec");
   return check_launch("slots_scatter");
 }
 

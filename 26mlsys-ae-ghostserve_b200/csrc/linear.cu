@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
     pipe::bar_init_fence();
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t vend = a.begin + (((a.end - a.begin) >> 4) << 4);  // end of the whole-vector part
   const int64_t items = (vend - a.begin + ITEM - 1) / ITEM;
 
@@ -170,8 +172,7 @@ int launch_xor(const LinearPass& a, cudaStream_t s, int ring_bytes) {
   per_sm = per_sm > 5 ? 5 : per_sm;
   const int64_t items = ((a.end - a.begin) / 16 * 16 + SPS * kLSeg - 1) / (SPS * kLSeg);
   const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
-  k<<<(int)grid, kLLanes + 32, smem, s>>>(a, nst);
-  return check_launch("xor_tma_kernel");
+  return launch_rc(launch_pdl(k, dim3((unsigned)grid), dim3(kLLanes + 32), smem, s, a, nst), "xor_tma_kernel");
 }
 
 // ------------------------------------------------- GF(2^8), fixed input count
@@ -197,6 +198,8 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
   __syncthreads();
   for (int w = threadIdx.x; w < NIN * 256 * R; w += blockDim.x) tab[w] = compact[w >> RSH];
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
 
   // Byte offset of this lane's replica inside an entry; entries are R*4 bytes
   // apart, so (data byte << log2(R*4)) | lane_off addresses a lookup with one
@@ -264,6 +267,8 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
 // --------------------------------------------------------------- GF(2^8) ----
 template <int NOUT, int R>
 __global__ void __launch_bounds__(1024) gf8_vec_kernel(const LinearPass a) {
+  grid_dep_wait();
+  grid_dep_launch();
   extern __shared__ uint32_t tab[];  // [nin][256][R]
   for (int e = threadIdx.x; e < a.nin * 256; e += blockDim.x) {
     const int i = e >> 8, x = e & 255;
@@ -322,6 +327,8 @@ __global__ void __launch_bounds__(1024) gf8_vec_kernel(const LinearPass a) {
 // input, entries pack the u16 products of outputs 0 (low half) and 1 (high).
 template <int NOUT, int R, bool U>
 __global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
+  grid_dep_wait();
+  grid_dep_launch();
   extern __shared__ uint32_t tab[];  // [nin][2][256][R]
   for (int e = threadIdx.x; e < a.nin * 512; e += blockDim.x) {
     const int i = e >> 9, h = (e >> 8) & 1, x = e & 255;
@@ -370,6 +377,8 @@ __global__ void __launch_bounds__(1024) gf16_vec_kernel(const LinearPass a) {
 // aligned sources): each thread XORs ldu16 windows of every input into an
 // aligned 16-byte store of every output. Contiguous shards only.
 __global__ void __launch_bounds__(256) xor_unaligned_kernel(const LinearPass a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t nvec = (a.end - a.begin) >> 4;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += step) {
@@ -385,6 +394,8 @@ __global__ void __launch_bounds__(256) xor_unaligned_kernel(const LinearPass a) 
 // ---------------------------------------------------------------- scalar ----
 // Misaligned layouts: one byte (XOR/GF8) or one u16 word (GF16) per thread.
 __global__ void __launch_bounds__(256) linear_scalar_kernel(const LinearPass a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int sym = (a.field == Field::GF16) ? 2 : 1;
   const int64_t nsym = (a.end - a.begin) / sym;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
@@ -441,7 +452,8 @@ int launch_gf8(const LinearPass& a, cudaStream_t s) {
   auto k = gf8_vec_kernel<NOUT, R>;
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
-  k<<<grid, threads, smem, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(k, dim3((unsigned)(grid)), dim3(threads), smem, s, a))
+    return launch_rc(lrc, "k");
   return check_launch("gf8_vec_kernel");
 }
 
@@ -451,7 +463,8 @@ int launch_gf16(const LinearPass& a, cudaStream_t s) {
   auto k = gf16_vec_kernel<NOUT, R, U>;
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
-  k<<<grid, threads, smem, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(k, dim3((unsigned)(grid)), dim3(threads), smem, s, a))
+    return launch_rc(lrc, "k");
   return check_launch("gf16_vec_kernel");
 }
 
@@ -462,8 +475,7 @@ int launch_gf8_fixed(const LinearPass& a, cudaStream_t s) {
   auto k = gf8_fixed_kernel<NIN>;
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
-  k<<<grid, threads, smem, s>>>(a);
-  return check_launch("gf8_fixed_kernel");
+  return launch_rc(launch_pdl(k, dim3(grid), dim3(threads), smem, s, a), "gf8_fixed_kernel");
 }
 
 template <int NOUT>
@@ -508,7 +520,8 @@ int run_scalar(const LinearPass& a, cudaStream_t s) {
   const int threads = 256;
   const int64_t nsym = (a.end - a.begin) / (a.field == Field::GF16 ? 2 : 1);
   const int grid = occupancy_grid(linear_scalar_kernel, threads, 0, nsym);
-  linear_scalar_kernel<<<grid, threads, 0, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(linear_scalar_kernel, dim3((unsigned)(grid)), dim3(threads), 0, s, a))
+    return launch_rc(lrc, "linear_scalar_kernel");
   return check_launch("linear_scalar_kernel");
 }
 
@@ -552,7 +565,8 @@ int run_unaligned(const LinearPass& a, cudaStream_t s) {
     if (a.field == Field::XOR) {
       const int threads = 256;
       const int grid = occupancy_grid(xor_unaligned_kernel, threads, 0, (b.end - b.begin) >> 4);
-      xor_unaligned_kernel<<<grid, threads, 0, s>>>(b);
+      if (const cudaError_t lrc = launch_pdl(xor_unaligned_kernel, dim3((unsigned)(grid)), dim3(threads), 0, s, b))
+        return launch_rc(lrc, "xor_unaligned_kernel");
       rc = check_launch("xor_unaligned_kernel");
     } else {
       if (b.nout > 2) return run_scalar(a, s);

@@ -50,6 +50,8 @@ __device__ __forceinline__ void st16(char* p, uint4 v) {
 // ---------------------------------------------------------------- encode ----
 template <int P>
 __global__ void __launch_bounds__(256) rdp_encode_kernel(const RdpEncodeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t lanes = a.unit >> 4;
   const int64_t stripe_bytes = (int64_t)(P - 1) * a.unit;
   const int64_t items = (a.s_end - a.s_begin) * lanes;
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const Rd
     pipe::bar_init_fence();
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t spu = a.unit / kSeg;
   const int64_t items = (a.s_end - a.s_begin) * spu;
   const int64_t sb = (int64_t)(P - 1) * a.unit;
@@ -186,6 +190,8 @@ __global__ void __launch_bounds__(kSegLanes + 32) rdp_encode_tma_kernel(const Rd
 // ---------------------------------------------------------------- decode ----
 template <int P>
 __global__ void __launch_bounds__(256) rdp_decode_kernel(const RdpDecodeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   constexpr int NS = 2 * (P - 1);
   const int64_t lanes = a.unit >> 4;
   const int64_t stripe_bytes = (int64_t)(P - 1) * a.unit;
@@ -266,6 +272,8 @@ __global__ void __launch_bounds__(kDecThreads) rdp_decode_tma_kernel(const RdpDe
     pipe::bar_init_fence();
   }
   __syncthreads();
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t spu = a.unit / kSeg;
   const int64_t items = (a.s_end - a.s_begin) * spu;
   const int64_t sb = (int64_t)(P - 1) * a.unit;
@@ -423,13 +431,14 @@ int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
     const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
-    k<<<(int)grid, kSegLanes + 32, smem, s>>>(a, nst);
-    return check_launch("rdp_encode_tma_kernel");
+    return launch_rc(launch_pdl(k, dim3((unsigned)grid), dim3(kSegLanes + 32), smem, s, a, nst),
+                     "rdp_encode_tma_kernel");
   }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
   const int threads = 256;
   const int grid = grid_for(rdp_encode_kernel<P>, threads, items);
-  rdp_encode_kernel<P><<<grid, threads, 0, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(rdp_encode_kernel<P>, dim3((unsigned)(grid)), dim3(threads), 0, s, a))
+    return launch_rc(lrc, "rdp_encode_kernel");
   return check_launch("rdp_encode_kernel");
 }
 template <int P>
@@ -447,13 +456,14 @@ int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
     per_sm = per_sm > kCtasPerSm ? kCtasPerSm : per_sm;
     const int64_t items = (a.s_end - a.s_begin) * (a.unit / kSeg);
     const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
-    k<<<(int)grid, kDecThreads, smem, s>>>(a, nst);
-    return check_launch("rdp_decode_tma_kernel");
+    return launch_rc(launch_pdl(k, dim3((unsigned)grid), dim3(kDecThreads), smem, s, a, nst),
+                     "rdp_decode_tma_kernel");
   }
   const int64_t items = (a.s_end - a.s_begin) * (a.unit >> 4);
   const int threads = 256;
   const int grid = grid_for(rdp_decode_kernel<P>, threads, items);
-  rdp_decode_kernel<P><<<grid, threads, 0, s>>>(a);
+  if (const cudaError_t lrc = launch_pdl(rdp_decode_kernel<P>, dim3((unsigned)(grid)), dim3(threads), 0, s, a))
+    return launch_rc(lrc, "rdp_decode_kernel");
   return check_launch("rdp_decode_kernel");
 }
 

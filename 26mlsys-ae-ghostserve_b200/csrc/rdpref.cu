@@ -79,6 +79,8 @@ __device__ __forceinline__ int64_t wrap_s(int64_t x, int64_t S) {
 // independent straight-line code (all in flight at once); ND = 0: any count.
 template <int ND>
 __global__ void __launch_bounds__(256) rdpref_parity_kernel(RdpRefParityArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int nd = ND > 0 ? ND : a.nd;
   const int64_t S = a.S;
   const int64_t nvec = (S + 7) >> 3;
@@ -157,6 +159,8 @@ __device__ __forceinline__ void ref_words(const RdpRefParityArgs& a, int64_t d, 
 }
 
 __global__ void __launch_bounds__(256) rdpref_parity_any(RdpRefParityArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int64_t S = a.S;
   const int64_t slots = (S >> 3) + 2;
   uint16_t* prow = a.rows + (int64_t)a.nd * a.pitch;
@@ -213,7 +217,8 @@ int rdpref_parity(uint16_t* rows, int64_t pitch, int nd, int64_t S, int star_bas
     int64_t grid = (2 * ((S >> 3) + 2) + threads - 1) / threads;
     const int64_t cap = (int64_t)sm_count() * 8;
     grid = grid > cap ? cap : (grid < 1 ? 1 : grid);
-    rdpref_parity_any<<<(int)grid, threads, 0, s>>>(a);
+    if (const cudaError_t lrc = launch_pdl(rdpref_parity_any, dim3((unsigned)((int)grid)), dim3(threads), 0, s, a))
+      return launch_rc(lrc, "rdpref_parity_any");
     return check_launch("rdpref_parity_any");
   }
   const int64_t nvec = (S + 7) >> 3;
@@ -222,14 +227,46 @@ int rdpref_parity(uint16_t* rows, int64_t pitch, int nd, int64_t S, int star_bas
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   switch (nd) {
-    case 2: rdpref_parity_kernel<2><<<(int)grid, threads, 0, s>>>(a); break;
-    case 3: rdpref_parity_kernel<3><<<(int)grid, threads, 0, s>>>(a); break;
-    case 4: rdpref_parity_kernel<4><<<(int)grid, threads, 0, s>>>(a); break;
-    case 5: rdpref_parity_kernel<5><<<(int)grid, threads, 0, s>>>(a); break;
-    case 6: rdpref_parity_kernel<6><<<(int)grid, threads, 0, s>>>(a); break;
-    case 7: rdpref_parity_kernel<7><<<(int)grid, threads, 0, s>>>(a); break;
-    case 8: rdpref_parity_kernel<8><<<(int)grid, threads, 0, s>>>(a); break;
-    default: rdpref_parity_kernel<0><<<(int)grid, threads, 0, s>>>(a); break;
+    case 2:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<2>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 3:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<3>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 4:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<4>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 5:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<5>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 6:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<6>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 7:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<7>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    case 8:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<8>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
+    default:
+      if (const cudaError_t lrc = launch_pdl(rdpref_parity_kernel<0>, dim3((unsigned)((int)grid)), dim3(threads), 0,
+                                             s, a))
+        return launch_rc(lrc, "rdpref_parity_kernel");
+      break;
   }
   return check_launch("rdpref_parity_kernel");
 }

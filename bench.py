@@ -236,7 +236,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="rdp_p7",
-                    choices=sorted(WORKLOADS) + ["prefill", "hook", "sweep", "refcompat"])
+                    choices=sorted(WORKLOADS) + ["prefill", "hook", "sweep", "refcompat", "peer_encode"])
     ap.add_argument("--sweep-tokens", default="256,2048,8192", help="sweep workload: chunk sizes in tokens")
     ap.add_argument("--hook-tokens", type=int, default=2048, help="hook workload: tokens per extend call")
     ap.add_argument("--hook-modes", default="fused,reference", help="hook workload: modes to time")
@@ -268,6 +268,9 @@ def main():
         return
     if args.workload == "refcompat":
         run_refcompat(args)
+        return
+    if args.workload == "peer_encode":
+        run_peer_encode(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -320,6 +323,7 @@ def main():
     step = g.codec.PreparedEncode(spec, data_ptrs, None, nbytes, nbytes, par_ptrs, 0, pbytes, sh)
     erased, rebuilt = [], []
     if args.op == "decode":
+        cap.wait_stream(stream)  # the shards' uploads precede the encode
         step()  # the parity the decode reads
         torch.cuda.synchronize()
         erased = list(range(min(m, k)))  # data shards 0..m-1 lost: the heaviest pattern
@@ -690,6 +694,55 @@ def run_refcompat(args):
             "higher_is_better": False, "steps": args.steps, "warmup": args.warmup,
             "data": "synthetic (seeded random fp16 words)", "config": {"workload": "refcompat"}, "calls": out}
     print(json.dumps(line), flush=True)
+
+
+def run_peer_encode(args):
+    """One process, two GPUs: the config-1 codeword with the N=2 placement of
+    the multi-GPU bench (shards 0, 2, 4 on GPU 0; 1, 3, 5 on GPU 1) encoded on
+    GPU 0, its kernel reading GPU 1's shards through peer access. The command
+    ncu profiles for the NVLink counters of the encode (ncu never runs on a
+    multi-rank command). Parity checked against the known-answer digest."""
+    import ctypes
+    import importlib
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        print(json.dumps({"workload": "peer_encode", "unavailable": "needs two visible GPUs"}))
+        return
+    g = importlib.import_module(PKG)
+    torch.cuda.set_device(0)
+    for d in (0, 1):
+        torch.zeros(1, device=f"cuda:{d}")
+    torch.cuda.set_device(0)
+    rc = ctypes.CDLL("libcudart.so.12").cudaDeviceEnablePeerAccess(1, 0)
+    if rc not in (0, 704):  # 704: already enabled
+        raise RuntimeError(f"cudaDeviceEnablePeerAccess(1) failed: {rc}")
+    wl = WORKLOADS["rdp_p7"]
+    rec, host = kat_case("rdp_p7")
+    spec = g.CodeSpec(wl["scheme"], wl["k"], wl["m"], wl["p"], wl["unit"])
+    nbytes = wl["shard"]
+    data = [torch.from_numpy(h).to(f"cuda:{j % 2}") for j, h in enumerate(host)]
+    pb = spec.parity_bytes(nbytes)
+    par = [torch.empty(pb, dtype=torch.uint8, device="cuda:0") for _ in range(spec.m)]
+    stream = torch.cuda.current_stream(0)
+    step = g.codec.PreparedEncode(spec, [t.data_ptr() for t in data], None, nbytes, nbytes,
+                                  [t.data_ptr() for t in par], 0, pb, int(stream.cuda_stream))
+    for _ in range(args.warmup):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(0)
+    ms = e0.elapsed_time(e1) / args.steps
+    remote = nbytes * sum(1 for j in range(spec.k) if j % 2)
+    verified = [sha256_dev(t) for t in par] == rec["parity_sha256"] and g.codec.device_status(clear=True) == 0
+    print(json.dumps({"workload": "peer_encode", "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(ms, 5), "remote_bytes": remote,
+                      "remote_gbs": round(remote / (ms * 1e-3) / 1e9, 1), "verified": verified,
+                      "note": "GPU 0 alone reads over NVLink (eager launches)"}), flush=True)
 
 
 def init_nccl():
