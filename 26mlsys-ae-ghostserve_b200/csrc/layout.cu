@@ -606,27 +606,19 @@ int slots_move(bool gather, void* const* pools, int npools, int64_t pitch, int64
   a.hi = two ? static_cast<char*>(hi) : a.lo;
   a.split = two ? split : INT64_MAX;
   const int threads = 256;
-  const int grid = grid_cap((row_bytes >> 4) * n * nplanes * npools, threads);
-  if (gather) {
-    if (slot_bytes == 8)
-      if (const cudaError_t lrc = launch_pdl(slots_vec<int64_t, true>, dim3((unsigned)(grid)), dim3(threads), 0, s,
-                                             a, static_cast<const int64_t*>(slots)))
-        return launch_rc(lrc, "slots_vec");
-    else
-      if (const cudaError_t lrc = launch_pdl(slots_vec<int32_t, true>, dim3((unsigned)(grid)), dim3(threads), 0, s,
-                                             a, static_cast<const int32_t*>(slots)))
-        return launch_rc(lrc, "slots_vec");
-    return check_launch("slots_gather");
-  }
-  if (slot_bytes == 8)
-    if (const cudaError_t lrc = launch_pdl(slots_vec<int64_t, false>, dim3((unsigned)(grid)), dim3(threads), 0, s, a,
-                                           static_cast<const int64_t*>(slots)))
-      return launch_rc(lrc, "slots_vec");
+  const dim3 grid((unsigned)grid_cap((row_bytes >> 4) * n * nplanes * npools, threads));
+  cudaError_t rc;
+  if (gather)
+    rc = slot_bytes == 8 ? launch_pdl(slots_vec<int64_t, true>, grid, dim3(threads), 0, s, a,
+                                      static_cast<const int64_t*>(slots))
+                         : launch_pdl(slots_vec<int32_t, true>, grid, dim3(threads), 0, s, a,
+                                      static_cast<const int32_t*>(slots));
   else
-    if (const cudaError_t lrc = launch_pdl(slots_vec<int32_t, false>, dim3((unsigned)(grid)), dim3(threads), 0, s, a,
-                                           static_cast<const int32_t*>(slots)))
-      return launch_rc(lrc, "slots_vec");
-  return check_launch("slots_scatter");
+    rc = slot_bytes == 8 ? launch_pdl(slots_vec<int64_t, false>, grid, dim3(threads), 0, s, a,
+                                      static_cast<const int64_t*>(slots))
+                         : launch_pdl(slots_vec<int32_t, false>, grid, dim3(threads), 0, s, a,
+                                      static_cast<const int32_t*>(slots));
+  return launch_rc(rc, gather ? "slots_gather" : "slots_scatter");
 }
 
 }  // namespace gsec

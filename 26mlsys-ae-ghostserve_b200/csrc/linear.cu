@@ -453,7 +453,7 @@ int launch_gf8(const LinearPass& a, cudaStream_t s) {
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
   if (const cudaError_t lrc = launch_pdl(k, dim3((unsigned)(grid)), dim3(threads), smem, s, a))
-    return launch_rc(lrc, "k");
+    return launch_rc(lrc, "gf8_vec_kernel");
   return check_launch("gf8_vec_kernel");
 }
 
@@ -464,7 +464,7 @@ int launch_gf16(const LinearPass& a, cudaStream_t s) {
   const int threads = 1024;
   const int grid = occupancy_grid(k, threads, smem, (a.end - a.begin) >> 4);
   if (const cudaError_t lrc = launch_pdl(k, dim3((unsigned)(grid)), dim3(threads), smem, s, a))
-    return launch_rc(lrc, "k");
+    return launch_rc(lrc, "gf16_vec_kernel");
   return check_launch("gf16_vec_kernel");
 }
 
