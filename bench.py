@@ -918,19 +918,34 @@ def run_sweep(args):
                 dec = g.codec.PreparedDecode(spec, ptrs, None, nbytes, nbytes, erased, 0, pbytes, sh)
                 enc_bytes = k * nbytes + m * pbytes
                 dec_bytes = k * nbytes + len(erased) * nbytes  # survivors read (k of them) + rebuilt written
+                # cold L2 (one GPU): R copies of the codeword, launches cycling through
+                # them, R x working set >= 384 MiB, so each launch's bytes were last
+                # touched >= 256 MiB of traffic earlier and have left the 126 MB L2
+                rot_enc, rot_dec, copies = [], [], []
+                ws = enc_bytes + len(erased) * nbytes
+                if world == 1 and ws < 256 * MIB:
+                    for _ in range(-(-384 * MIB // ws)):
+                        cd = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(k)]
+                        cp = [torch.empty(pbytes, dtype=torch.uint8, device=device) for _ in range(m)]
+                        cr = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in erased]
+                        copies.append((cd, cp, cr))
+                        rot_enc.append(g.codec.PreparedEncode(spec, [t.data_ptr() for t in cd], None, nbytes, nbytes,
+                                                              [t.data_ptr() for t in cp], 0, pbytes, sh))
+                        cptrs = [t.data_ptr() for t in cd] + [t.data_ptr() for t in cp]
+                        for e, t in zip(erased, cr):
+                            cptrs[e] = t.data_ptr()
+                        rot_dec.append(g.codec.PreparedDecode(spec, cptrs, None, nbytes, nbytes, erased, 0, pbytes,
+                                                              sh))
 
-                def timed(fn, est_bytes):
-                    # reps launches captured in one CUDA graph: device time, not host launch rate
-                    reps = max(5, min(200, int(0.02 / (est_bytes / 5e12))))
-                    cap.wait_stream(stream)
-                    for _ in range(3):
-                        fn()
+                def graph_ms(fns, reps):
+                    """Device ms of reps x fns replayed from one CUDA graph (warm replay first)."""
                     graph = torch.cuda.CUDAGraph()
                     with torch.cuda.graph(graph, stream=cap):
                         for _ in range(reps):
-                            fn()
+                            for f in fns:
+                                f()
                     torch.cuda.synchronize()
-                    graph.replay()  # warm
+                    graph.replay()  # warm: uploads the graph
                     torch.cuda.synchronize()
                     if world > 1:
                         dist.barrier()
@@ -940,15 +955,32 @@ def run_sweep(args):
                     e1.record(stream)
                     torch.cuda.synchronize()
                     del graph
-                    t = torch.tensor([e0.elapsed_time(e1) / reps], device=device, dtype=torch.float64)
+                    return e0.elapsed_time(e1)
+
+                def timed(fn, rot, est_bytes):
+                    """(hot, cold) ms per launch. hot: back-to-back launches of
+                    one codeword (a working set under the 126 MB L2 is partly
+                    served from it); cold: back-to-back launches cycling through
+                    the rotating copies (same as hot when there are none). Max
+                    over ranks."""
+                    reps = max(5, min(200, int(0.02 / (est_bytes / 5e12))))
+                    cap.wait_stream(stream)
+                    for _ in range(3):
+                        fn()
+                    hot = graph_ms([fn], reps) / reps
+                    cold = hot
+                    if rot:
+                        creps = max(1, -(-reps // len(rot)))
+                        cold = graph_ms(rot, creps) / (creps * len(rot))
+                    t = torch.tensor([hot, cold], device=device, dtype=torch.float64)
                     if world > 1:
                         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                    return float(t.item())
+                    return float(t[0].item()), float(t[1].item())
 
                 if world > 1:
                     dist.barrier()
-                ms_e = timed(enc, enc_bytes)
-                ms_d = timed(dec, dec_bytes)
+                ms_e, cms_e = timed(enc, rot_enc, enc_bytes)
+                ms_d, cms_d = timed(dec, rot_dec, dec_bytes)
                 ok = all(torch.equal(t, slots[e]) for e, t in zip(erased, rebuilt)) if world == 1 else None
                 if world > 1:  # the rebuilt shards are copies of (possibly remote) shards: compare there
                     flags = torch.tensor([0], device=device)
@@ -965,6 +997,8 @@ def run_sweep(args):
                        "enc_frac": round(enc_bytes / (ms_e * 1e-3) / 1e9 / peak, 3),
                        "dec_gbs": round(dec_bytes / (ms_d * 1e-3) / 1e9, 1),
                        "dec_frac": round(dec_bytes / (ms_d * 1e-3) / 1e9 / peak, 3),
+                       "cold_enc_frac": round(enc_bytes / (cms_e * 1e-3) / 1e9 / peak, 3),
+                       "cold_dec_frac": round(dec_bytes / (cms_d * 1e-3) / 1e9 / peak, 3),
                        "erased": erased, "verified": ok}
                 if world > 1:
                     link = 770.0
@@ -979,7 +1013,7 @@ def run_sweep(args):
                     torch.cuda.synchronize()
                     dist.barrier()
                     group.close()
-                del slots, parity, rebuilt
+                del slots, parity, rebuilt, copies, rot_enc, rot_dec
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             wl = dict(scheme=scheme, k=k, m=m, p=p, unit=4096 if scheme == "rdp" else 0, shard=16 * MIB, kv="u8")
             rng = np.random.default_rng(k)
@@ -993,7 +1027,11 @@ def run_sweep(args):
                 "scaling": "weak", "dtype": "u8", "data": "synthetic (uniform random bytes)",
                 "peak": peak, "peak_kind": peak_kind,
                 "config": {"workload": "sweep", "tokens": tokens_list,
-                           "shard": "tokens x 32 layers x 1 kv head x 128 x (K,V) x (2 B bf16 | 1 B fp8)"},
+                           "shard": "tokens x 32 layers x 1 kv head x 128 x (K,V) x (2 B bf16 | 1 B fp8)",
+                           "l2": "enc/dec_frac: back-to-back launches of one codeword (working sets under the "
+                                 "126 MB L2 partly cached); cold_*: back-to-back launches cycling through copies "
+                                 "of the codeword totalling >= 384 MiB, so no launch finds its bytes in L2 (one "
+                                 "GPU; working sets >= 256 MiB and N > 1: same as back-to-back)"},
                 "rows": rows, "cpu_port": cpu_rates or None}
         print(json.dumps(line), flush=True)
     dist.barrier()
