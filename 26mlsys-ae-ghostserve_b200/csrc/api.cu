@@ -249,9 +249,10 @@ int gsec_device_status(uint32_t* status, int32_t clear) {
   const unsigned v1 = rdp_device_status(clear != 0);
   const unsigned v2 = linear_device_status(clear != 0);
   const unsigned v3 = layout_device_status(clear != 0);
-  const unsigned v = (v1 == 0xffffffffu || v2 == 0xffffffffu || v3 == 0xffffffffu)
+  const unsigned v4 = gather_device_status(clear != 0);
+  const unsigned v = (v1 == 0xffffffffu || v2 == 0xffffffffu || v3 == 0xffffffffu || v4 == 0xffffffffu)
                          ? 0xffffffffu
-                         : (v1 | (v2 << 8) | (v3 << 16));
+                         : (v1 | (v2 << 8) | (v3 << 16) | (v4 << 24));
   if (v == 0xffffffffu) {
     set_error("cannot read the device status word");
     return GSEC_ECUDA;

@@ -15,6 +15,7 @@
 // 16-byte aligned; otherwise one byte (or u16 word) per thread.
 #include "common.cuh"
 #include "layout.cuh"
+#include "pipe.cuh"
 
 namespace gsec {
 namespace {
@@ -496,39 +497,80 @@ __global__ void slots_vec(const SlotArgs a, const I* slots) {
 }  // namespace
 
 // --------------------------------------------------- gather of n buffers --
-// dst = src[0][0..bytes[0]) ++ src[1][0..bytes[1]) ++ ... with 16-byte loads,
-// four in flight per thread. The sources may be mapped peer buffers, so this
-// is also the plain peer-read copy that bench.py times as the NVLink ceiling of
-// a placement (the encode kernels read the same bytes with bulk copies).
+// dst = src[0][0..bytes[0]) ++ src[1][0..bytes[1]) ++ ... moved by bulk copies:
+// each CTA's one active thread pulls 16 KiB chunks of the sources into a ring
+// of shared-memory stages (cp.async.bulk, no multicast) and pushes each back
+// out with a bulk store, four chunks in flight per CTA. The sources may be
+// mapped peer buffers, so this is also the plain peer-read copy that bench.py
+// times as the NVLink ceiling of a shard placement: the same copy engine the
+// encode kernels' producer warps use, with no arithmetic behind it.
+static __device__ unsigned g_gather_status;
+
 namespace {
 constexpr int kGatherMax = 32;
+constexpr int kGChunk = 16384;
+constexpr int kGStages = 4;
 struct GatherArgs {
   const char* src[kGatherMax];
-  int64_t vend[kGatherMax];  // cumulative 16-byte vector counts
+  int64_t bytes[kGatherMax];
+  int64_t item_end[kGatherMax];  // cumulative chunk counts
+  int64_t dst_off[kGatherMax];   // byte offset of source i in dst
   int n;
   char* dst;
 };
 
-__device__ __forceinline__ const char* gather_src(const GatherArgs& a, int64_t v) {
+__device__ __forceinline__ void gather_item(const GatherArgs& a, int64_t it, const char*& src, char*& dst,
+                                            uint32_t& len) {
   int i = 0;
-  while (i + 1 < a.n && v >= a.vend[i]) ++i;
-  return a.src[i] + ((v - (i ? a.vend[i - 1] : 0)) << 4);
+  while (i + 1 < a.n && it >= a.item_end[i]) ++i;
+  const int64_t c = it - (i ? a.item_end[i - 1] : 0);
+  const int64_t off = c * kGChunk;
+  const int64_t rest = a.bytes[i] - off;
+  len = (uint32_t)(rest < kGChunk ? rest : kGChunk);
+  src = a.src[i] + off;
+  dst = a.dst + a.dst_off[i] + off;
 }
 
-__global__ void __launch_bounds__(256) gather_vec(const GatherArgs a) {
+__global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * kGChunk);
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kGStages; ++st) pipe::bar_init(full + st, 1);
+    pipe::bar_init_fence();
+  }
+  __syncwarp();
   grid_dep_wait();
   grid_dep_launch();
-  const int64_t total = a.vend[a.n - 1];
-  const int64_t step = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += 4 * step) {
-    uint4 x[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (v + u * step < total) x[u] = ldv(gather_src(a, v + u * step));
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (v + u * step < total) stv(a.dst + ((v + u * step) << 4), x[u]);
+  if (threadIdx.x != 0) return;
+  const int64_t items = a.item_end[a.n - 1];
+  const char* src;
+  char* dst;
+  uint32_t len;
+  // prologue: the first kGStages chunks of this CTA in flight
+  int64_t it = blockIdx.x;
+  for (int st = 0; st < kGStages && it + (int64_t)st * gridDim.x < items; ++st) {
+    gather_item(a, it + (int64_t)st * gridDim.x, src, dst, len);
+    pipe::bar_expect_tx(full + st, len);
+    pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
   }
+  for (int64_t k = 0; it < items; ++k, it += gridDim.x) {
+    const int st = (int)(k % kGStages);
+    if (!pipe::bar_wait(full + st, (uint32_t)((k / kGStages) & 1))) {
+      atomicOr(&g_gather_status, 1u);
+      break;
+    }
+    gather_item(a, it, src, dst, len);
+    pipe::bulk_store(dst, smem + st * kGChunk, len);
+    pipe::bulk_commit();
+    const int64_t next = it + (int64_t)kGStages * gridDim.x;
+    if (next < items) {
+      pipe::bulk_wait_read_all();  // the stage's store has read it: refill
+      gather_item(a, next, src, dst, len);
+      pipe::bar_expect_tx(full + st, len);
+      pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
+    }
+  }
+  pipe::bulk_wait_all();
 }
 }  // namespace
 
@@ -540,26 +582,40 @@ int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, 
   GatherArgs a{};
   a.n = n;
   a.dst = static_cast<char*>(dst);
-  int64_t acc = 0;
+  int64_t items = 0, off = 0;
   for (int i = 0; i < n; ++i) {
     if (bytes[i] < 0 || (bytes[i] & 15) || (bytes[i] && (!src[i] || !aligned16(src[i])))) {
       set_error("gather: source %d must be 16-byte aligned with a size that is a multiple of 16", i);
       return GSEC_EINVAL;
     }
     a.src[i] = static_cast<const char*>(src[i]);
-    acc += bytes[i] >> 4;
-    a.vend[i] = acc;
+    a.bytes[i] = bytes[i];
+    a.dst_off[i] = off;
+    off += bytes[i];
+    items += (bytes[i] + kGChunk - 1) / kGChunk;
+    a.item_end[i] = items;
   }
-  if (acc == 0) return GSEC_OK;
+  if (items == 0) return GSEC_OK;
   if (!dst || !aligned16(dst)) {
     set_error("gather: destination must be 16-byte aligned");
     return GSEC_EINVAL;
   }
-  const int threads = 256;
-  if (const cudaError_t lrc = launch_pdl(gather_vec, dim3((unsigned)(grid_cap((acc + 3) / 4, threads))),
-                                         dim3(threads), 0, s, a))
-    return launch_rc(lrc, "gather_vec");
-  return check_launch("gather_vec");
+  const size_t smem = (size_t)kGStages * kGChunk + kGStages * sizeof(uint64_t);
+  LaunchCache& cache = launch_cache();
+  const int per_sm = cache.blocks_per_sm(gather_bulk, 32, smem);
+  if (per_sm < 0) return check_launch("gather_bulk launch shape");
+  const int64_t grid = balanced_grid(items, (int64_t)sm_count() * per_sm);
+  return launch_rc(launch_pdl(gather_bulk, dim3((unsigned)grid), dim3(32), smem, s, a), "gather_bulk");
+}
+
+unsigned gather_device_status(bool clear) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gather_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_gather_status, &z, sizeof(z));
+  }
+  return v;
 }
 
 unsigned layout_device_status(bool clear) {

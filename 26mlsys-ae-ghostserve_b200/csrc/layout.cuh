@@ -22,5 +22,7 @@ int slots_move(bool gather, void* const* pools, int npools, int64_t pitch, int64
 // Status word of the slot kernels (bit 0: a slot past the pool's rows).
 int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, cudaStream_t s);
 unsigned layout_device_status(bool clear);
+// Status word of the gather kernel (bit 0: a bounded wait gave up).
+unsigned gather_device_status(bool clear);
 
 }  // namespace gsec

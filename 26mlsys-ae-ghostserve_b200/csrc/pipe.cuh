@@ -79,6 +79,21 @@ __device__ __forceinline__ void bulk_load_split(void* dst, const char* lo, const
   }
 }
 
+// Bulk copy of `bytes` (multiple of 16, 16-byte aligned ends) from this CTA's
+// shared memory to global memory, as one member of the current bulk group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store has read its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Consumer side: every lane of the warp has finished reading the stage; one
 // arrival per warp (the empty barrier counts warps).
 __device__ __forceinline__ void warp_release(uint64_t* b) {

@@ -482,9 +482,10 @@ def hashlib_np(a) -> str:
 
 
 def measure_peer_read(torch, g, peer_group, remote, nbytes, device, stream, max_over_ranks, barrier):
-    """GB/s per direction of a plain copy kernel (gsec_copy_gather, 16-byte
-    loads) that reads this rank's remote shards (the same bytes the encode
-    reads over NVLink) into local memory, all ranks at once, max over ranks."""
+    """GB/s per direction of a plain copy kernel (gsec_copy_gather: bulk copies
+    through shared memory, no arithmetic) that reads this rank's remote shards
+    (the same bytes the encode reads over NVLink) into local memory, all ranks
+    at once, max over ranks."""
     if not remote:
         return None
     L = g._lib
@@ -509,7 +510,7 @@ def measure_peer_read(torch, g, peer_group, remote, nbytes, device, stream, max_
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / reps)
     barrier()
-    return {"gbs": round(nbytes * len(remote) / (ms * 1e-3) / 1e9, 1), "kernel": "gather_vec (gsec_copy_gather)",
+    return {"gbs": round(nbytes * len(remote) / (ms * 1e-3) / 1e9, 1), "kernel": "gather_bulk (gsec_copy_gather)",
             "bytes": nbytes * len(remote), "reps": reps}
 
 
@@ -1001,12 +1002,12 @@ def run_sweep(args):
                        "cold_dec_frac": round(dec_bytes / (cms_d * 1e-3) / 1e9 / peak, 3),
                        "erased": erased, "verified": ok}
                 if world > 1:
-                    link = 770.0
+                    link = 900.0  # NVLink-5, GB/s per direction per GPU
                     # the decode reads only the survivors: the lost shards' remote bytes do not cross NVLink
                     dec_remote = sum(nbytes for j in range(k) if j not in erased and (rank + j) % world != rank)
                     for key, ms, tot, rem in (("enc", ms_e, enc_bytes, remote), ("dec", ms_d, dec_bytes, dec_remote)):
                         roof = max((tot - rem) / (peak * 1e9), rem / (link * 1e9))
-                        row[key + "_roof_frac"] = round(roof * 1e3 / ms, 3)
+                        row[key + "_roof_frac"] = round(roof * 1e3 / ms, 3)  # of max(HBM, 900 GB/s link)
                     row["remote_bytes"] = remote
                 rows.append(row)
                 if group is not None:

@@ -156,10 +156,12 @@ GSEC_API int gsec_slots_scatter(void* pool, int64_t pitch, int64_t plane, int32_
 
 /* One-kernel gather: dst = src[0][0..bytes[0]) ++ ... ++ src[n-1][0..bytes[n-1])
  * (n <= 32; every source, size and dst 16-byte aligned/multiple of 16). Sources
- * may be mapped peer buffers: this is a plain peer-read copy (16-byte loads),
- * the copy the reference hook does with two NCCL gathers to one rank
- * (bench_ghostserve_rdp.py:303-332) done as reads by the destination GPU;
- * bench.py times it as the NVLink read ceiling of a shard placement. */
+ * may be mapped peer buffers: this is a plain peer-read copy (bulk copies
+ * through shared memory, no arithmetic), the copy the reference hook does with
+ * two NCCL gathers to one rank (bench_ghostserve_rdp.py:303-332) done as reads
+ * by the destination GPU; bench.py times it as the NVLink read ceiling of a
+ * shard placement. A bounded wait that gives up sets bit 24 of
+ * gsec_device_status. */
 GSEC_API int gsec_copy_gather(const void* const* src, const int64_t* bytes, int32_t n, void* dst,
                               gsec_stream_t stream);
 

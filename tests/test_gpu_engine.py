@@ -292,3 +292,19 @@ def test_slots_gather_rejects_bad_arguments():
         codec.slots_gather(wide[:, :, :, :64], torch.arange(4, device="cuda"), out)  # rows not contiguous
     with pytest.raises(ValueError):
         codec.slots_gather(pool, torch.arange(4, device="cuda"), out[1:])  # misaligned buffer
+
+
+# ------------------------------------------------------------ bulk gather ---
+@pytest.mark.parametrize("sizes", [[16], [0, 48, 16384], [16384 * 3 + 32, 7 * 16, 65536, 0, 16400], [1 << 20] * 5])
+def test_copy_gather_concatenates(sizes):
+    L = pkg("_lib")
+    g = torch.Generator(device="cuda").manual_seed(len(sizes))
+    srcs = [torch.randint(0, 256, (max(n, 16),), generator=g, device="cuda", dtype=torch.uint8) for n in sizes]
+    dst = torch.full((sum(sizes) + 64,), 7, dtype=torch.uint8, device="cuda")
+    ptrs = L.ptr_array([t.data_ptr() for t in srcs])
+    nb = (L.C.c_int64 * len(sizes))(*sizes)
+    L.call("gsec_copy_gather", ptrs, nb, len(sizes), L.C.c_void_p(dst.data_ptr()),
+           L.C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    want = torch.cat([t[:n] for t, n in zip(srcs, sizes)])
+    assert torch.equal(dst[:sum(sizes)], want)
+    assert int((dst[sum(sizes):] == 7).sum()) == 64  # nothing past the end

@@ -192,3 +192,17 @@ def test_slots_gather_rejects_host_tensors():
     pool = torch.zeros(8, 2, 1, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         c.slots_gather(pool, torch.arange(4), torch.empty(4096, dtype=torch.uint8))
+
+
+def test_copy_gather_argument_checks_run_on_host():
+    """Rejected before any launch: source count, a source size that is not a
+    multiple of 16, a null source (null pointers only, so nothing is launched)."""
+    L = pkg("_lib")
+    sizes = (ctypes.c_int64 * 2)(32, 32)
+    with pytest.raises(ValueError, match="sources"):
+        L.call("gsec_copy_gather", L.ptr_array([0, 0]), sizes, 0, None, None)
+    with pytest.raises(ValueError, match="16"):
+        L.call("gsec_copy_gather", L.ptr_array([0, 0]), (ctypes.c_int64 * 2)(8, 32), 2, None, None)
+    with pytest.raises(ValueError, match="aligned"):
+        L.call("gsec_copy_gather", L.ptr_array([0, 0]), sizes, 2, None, None)
+    L.call("gsec_copy_gather", L.ptr_array([0]), (ctypes.c_int64 * 1)(0), 1, None, None)  # nothing to copy
