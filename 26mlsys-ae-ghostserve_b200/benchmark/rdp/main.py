@@ -21,8 +21,17 @@ import sys
 
 import torch
 
-from ... import _lib
-from ...codec import stream_handle
+if __package__ in (None, ""):  # run as a script (cd benchmark/rdp; python main.py ...), as the reference's demo is
+    import importlib as _importlib
+    import os as _os
+
+    sys.path.insert(0, _os.path.dirname(_os.path.dirname(_os.path.dirname(_os.path.dirname(
+        _os.path.abspath(__file__))))))
+    __package__ = "26mlsys-ae-ghostserve_b200.benchmark.rdp"
+    _importlib.import_module(__package__)
+
+from ... import _lib  # noqa: E402
+from ...codec import stream_handle  # noqa: E402
 
 
 def _s():

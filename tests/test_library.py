@@ -206,3 +206,16 @@ def test_copy_gather_argument_checks_run_on_host():
     with pytest.raises(ValueError, match="aligned"):
         L.call("gsec_copy_gather", L.ptr_array([0, 0]), sizes, 2, None, None)
     L.call("gsec_copy_gather", L.ptr_array([0]), (ctypes.c_int64 * 1)(0), 1, None, None)  # nothing to copy
+
+
+@pytest.mark.parametrize("sub", ["xor", "rdp", "rs"])
+def test_dropin_demo_runs_as_a_script(sub):
+    """The reference runs its demos as `cd benchmark/<code>; python main.py`;
+    the drop-ins start the same way (argument parsing needs no GPU)."""
+    import subprocess
+    import sys
+
+    d = os.path.join(ROOT, "26mlsys-ae-ghostserve_b200", "benchmark", sub)
+    r = subprocess.run([sys.executable, "main.py", "--help"], cwd=d, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "--num_data_shards" in r.stdout
