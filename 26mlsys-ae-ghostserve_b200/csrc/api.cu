@@ -555,6 +555,25 @@ int gsec_xor_encode(const uint8_t* data_padded, uint8_t* shards, int32_t data_sh
                kLinMaxIn);
   GSEC_REQUIRE(shard_size >= 1 && pitch >= shard_size, "bad shard_size/pitch");
   const cudaStream_t s = as_stream(stream);
+  const bool rows_aligned = aligned16(shards) && shard_size % 16 == 0 && pitch % 16 == 0 &&
+                            (data_padded == nullptr || aligned16(data_padded));
+  if (!rows_aligned && pitch == shard_size && (data_padded == nullptr || aligned16(data_padded)) &&
+      aligned16(shards)) {
+    // rows at any byte offset, back to back: the data rows are one flat copy and
+    // the parity row one XOR pass over windows of them -- a single launch
+    RowCopyXor r;
+    const char* src = data_padded ? reinterpret_cast<const char*>(data_padded) : reinterpret_cast<const char*>(shards);
+    if (data_padded) {
+      r.src = src;
+      r.dst = reinterpret_cast<char*>(shards);
+      r.copy_len = (int64_t)data_shards * shard_size;
+    }
+    r.nin = data_shards;
+    for (int i = 0; i < data_shards; ++i) r.in[i] = src + (int64_t)i * shard_size;
+    r.out0 = reinterpret_cast<char*>(shards) + (int64_t)data_shards * shard_size;
+    r.len = shard_size;
+    return run_row_copy_xor(r, s);
+  }
   if (data_padded) {
     int rc = rows_pack(data_padded, (int64_t)data_shards * shard_size, nullptr, 0, shards, pitch, shard_size,
                        data_shards, s);
@@ -661,6 +680,34 @@ int gsec_rdpref_recovery(uint16_t* shards, int64_t pitch_words, uint16_t* out_tn
   GSEC_REQUIRE(shards && out_tn && nd >= 1 && nd + 1 <= kLinMaxIn && S >= 1 && pitch_words >= S, "bad arguments");
   GSEC_REQUIRE((int64_t)nd * S >= 2 * T * n, "nd * S < 2 * T * n");
   const cudaStream_t s = as_stream(stream);
+  if (pitch_words == S && S % 8 != 0 && aligned16(shards) && aligned16(out_tn)) {
+    // rows back to back at any byte offset: the token stream is the first 4Tn
+    // bytes of the rows, so one launch rebuilds the lost row in place (P and
+    // the other rows read through windows), writes it into the stream too, and
+    // copies the other rows' bytes of the stream
+    const int target = rdpref_target(nd, miss_a, miss_b);
+    const char* base = reinterpret_cast<const char*>(shards);
+    const int64_t row = 2 * S;
+    RowCopyXor r;
+    r.src = base;
+    r.dst = reinterpret_cast<char*>(out_tn);
+    r.copy_len = 4 * T * n;
+    if (target >= 0) {
+      r.skip_lo = target * row;
+      r.skip_hi = (target + 1) * row;
+      for (int i = 0; i <= nd; ++i)
+        if (i != target) r.in[r.nin++] = base + i * row;  // the other data rows and P (row nd)
+      r.out0 = reinterpret_cast<char*>(shards) + target * row;
+      r.out1 = reinterpret_cast<char*>(out_tn) + target * row;
+      r.out1_len = r.copy_len - target * row;
+      if (r.out1_len < 0) r.out1_len = 0;
+      r.len = row;
+    } else {
+      r.nin = 1;  // nothing to rebuild: the copy alone
+      r.in[0] = base;
+    }
+    return run_row_copy_xor(r, s);
+  }
   int rc = rdpref_rebuild(shards, pitch_words, nd, S, rdpref_target(nd, miss_a, miss_b), s);
   if (rc) return rc;
   if (T * n == 0) return GSEC_OK;

@@ -530,6 +530,77 @@ constexpr int64_t kTableBudget = 192 * 1024;
 
 }  // namespace
 
+namespace {
+// XOR of byte c of every input (a row's head/tail bytes).
+__device__ __forceinline__ char xor_byte(const RowCopyXor& a, int64_t c) {
+  unsigned char v = 0;
+  for (int r = 0; r < a.nin; ++r) v ^= static_cast<unsigned char>(a.in[r][c]);
+  return static_cast<char>(v);
+}
+
+__global__ void __launch_bounds__(256) row_copy_xor_kernel(const RowCopyXor a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t ncopy = (a.copy_len + 15) >> 4;
+  const uintptr_t first = reinterpret_cast<uintptr_t>(a.out0);
+  const int64_t head = a.len > 0 ? (int64_t)(first & 15u) : 0;  // out0's offset in its aligned block
+  char* base = reinterpret_cast<char*>(first - (uintptr_t)head);
+  const int64_t nblk = a.len > 0 ? (head + a.len + 15) >> 4 : 0;
+  const int64_t total = ncopy + nblk;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += step) {
+    if (v < ncopy) {  // the copy: aligned vectors, bytes near the skipped range or the end one by one
+      const int64_t o = v << 4;
+      if (o + 16 <= a.copy_len && (o + 16 <= a.skip_lo || o >= a.skip_hi)) {
+        st16(a.dst + o, ld16(a.src + o));
+      } else {
+        for (int b = 0; b < 16; ++b) {
+          const int64_t x = o + b;
+          if (x < a.copy_len && (x < a.skip_lo || x >= a.skip_hi)) a.dst[x] = a.src[x];
+        }
+      }
+      continue;
+    }
+    // the XOR row: aligned 16-byte blocks of out0 (out1 shares its alignment),
+    // inputs read through ldu16 windows; a partial first or last block bytewise
+    const int64_t col = ((v - ncopy) << 4) - head;  // column of the block's first byte
+    if (col >= 0 && col + 16 <= a.len) {
+      uint4 x = vzero();
+      for (int r = 0; r < a.nin; ++r) x = vxor(x, ldu16(a.in[r] + col));
+      st16(base + head + col, x);
+      if (a.out1 != nullptr) {
+        if (col + 16 <= a.out1_len)
+          st16(a.out1 + col, x);
+        else
+          for (int b = 0; b < 16 && col + b < a.out1_len; ++b) a.out1[col + b] = xor_byte(a, col + b);
+      }
+    } else {
+      for (int b = 0; b < 16; ++b) {
+        const int64_t c = col + b;
+        if (c < 0 || c >= a.len) continue;
+        const char val = xor_byte(a, c);
+        a.out0[c] = val;
+        if (a.out1 != nullptr && c < a.out1_len) a.out1[c] = val;
+      }
+    }
+  }
+}
+}  // namespace
+
+int run_row_copy_xor(const RowCopyXor& a, cudaStream_t s) {
+  if (a.copy_len <= 0 && a.len <= 0) return GSEC_OK;
+  if (a.nin < 1 || a.nin > kLinMaxIn || (a.copy_len > 0 && (!aligned16(a.src) || !aligned16(a.dst))) ||
+      (a.out1 != nullptr && ((reinterpret_cast<uintptr_t>(a.out1) ^ reinterpret_cast<uintptr_t>(a.out0)) & 15u))) {
+    set_error("row copy + XOR: bad inputs or alignment");
+    return GSEC_EINVAL;
+  }
+  const int threads = 256;
+  const int64_t work = ((a.copy_len + 15) >> 4) + ((a.len + 31) >> 4);
+  const int grid = occupancy_grid(row_copy_xor_kernel, threads, 0, work);
+  return launch_rc(launch_pdl(row_copy_xor_kernel, dim3((unsigned)grid), dim3(threads), 0, s, a),
+                   "row_copy_xor_kernel");
+}
+
 unsigned linear_device_status(bool clear) {
   unsigned v = 0;
   if (cudaMemcpyFromSymbol(&v, g_linear_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;

@@ -33,6 +33,27 @@ struct LinearPass {
   uint32_t unity = 1;  // always 1; read from the launch parameters, so the compiler cannot fold it
 };
 
+// One launch that copies src[0..copy_len) to dst (bytes in [skip_lo, skip_hi)
+// left to the XOR row) and writes one XOR row: out0[c] (and out1[c] for
+// c < out1_len) = XOR_r in[r][c] for c in [0, len). src, dst and out1 - out0
+// distance-compatible: src, dst 16-byte aligned, out1 with out0's alignment.
+// The reference-layout calls whose shard rows start at any byte offset use it:
+// encode_xor (data rows copied, parity row built) and the mod-S recovery
+// (lost row rebuilt in place, all rows unpacked to the token stream).
+struct RowCopyXor {
+  const char* src = nullptr;
+  char* dst = nullptr;
+  int64_t copy_len = 0;
+  int64_t skip_lo = 0, skip_hi = 0;
+  const char* in[kLinMaxIn] = {};
+  int nin = 0;
+  char* out0 = nullptr;
+  char* out1 = nullptr;
+  int64_t out1_len = 0;
+  int64_t len = 0;
+};
+int run_row_copy_xor(const RowCopyXor& a, cudaStream_t stream);
+
 // Device status word of the staged linear kernels (non-zero: a bounded wait gave up).
 unsigned linear_device_status(bool clear);
 
