@@ -159,26 +159,36 @@ __global__ void __launch_bounds__(kLLanes + 32) xor_tma_kernel(const LinearPass 
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, vend);
 }
 
-// One XOR input: the parity is a copy of it (the mirror of a one-data-shard
-// code). A plain streaming copy with four independent 16-byte loads in flight
-// per thread keeps more bytes in flight than a staging ring needs to and runs
-// at the copy peak; the ring kernel spends its time on barrier hand-offs here.
-__global__ void __launch_bounds__(256) xor_copy_kernel(const LinearPass a) {
+// Few XOR inputs (one: the parity is a copy, the mirror of a one-data-shard
+// code): a plain streaming kernel with four independent 16-byte vectors of
+// every input in flight per thread keeps more bytes in flight than a staging
+// ring needs to; the ring kernel spends its time on barrier hand-offs here.
+#ifndef GSEC_XOR_STREAM_MAXIN
+#define GSEC_XOR_STREAM_MAXIN 3
+#endif
+template <int NIN>
+__global__ void __launch_bounds__(256) xor_stream_kernel(const LinearPass a) {
   grid_dep_wait();
   grid_dep_launch();
   const int64_t nvec = (a.end - a.begin) >> 4;
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 4 * step) {
-    uint4 x[4];
+    uint4 x[4][NIN];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (v + u * step < nvec) x[u] = ld16(seg(a.in_lo[0], a.in_hi[0], a.split, a.begin + ((v + u * step) << 4)));
+#pragma unroll
+      for (int i = 0; i < NIN; ++i)
+        if (v + u * step < nvec) x[u][i] = ld16(seg(a.in_lo[i], a.in_hi[i], a.split, a.begin + ((v + u * step) << 4)));
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int64_t off = a.begin + ((v + u * step) << 4);
-      if (v + u * step < nvec)
+      if (v + u * step < nvec) {
+        uint4 acc = x[u][0];
+#pragma unroll
+        for (int i = 1; i < NIN; ++i) acc = vxor(acc, x[u][i]);
         for (int o = 0; o < a.nout; ++o)
-          if (off + 16 <= a.out_end[o]) st16(seg(a.out_lo[o], a.out_hi[o], a.split, off), x[u]);
+          if (off + 16 <= a.out_end[o]) st16(seg(a.out_lo[o], a.out_hi[o], a.split, off), acc);
+      }
     }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
@@ -686,10 +696,12 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
     case Field::XOR:
       // measured: 2-3 inputs run best with 4 KiB stages and a 36 KiB ring, one
       // input with 4 KiB stages and the default ring, more inputs with 1 KiB stages
-      if (a.nin == 1) {
+      if (a.nin <= GSEC_XOR_STREAM_MAXIN) {
         const int threads = 256;
-        const int grid = occupancy_grid(xor_copy_kernel, threads, 0, (((a.end - a.begin) >> 4) + 3) / 4);
-        return launch_rc(launch_pdl(xor_copy_kernel, dim3((unsigned)grid), dim3(threads), 0, s, a), "xor_copy_kernel");
+        const int64_t work = (((a.end - a.begin) >> 4) + 3) / 4;
+        auto k = a.nin == 1 ? xor_stream_kernel<1> : (a.nin == 2 ? xor_stream_kernel<2> : xor_stream_kernel<3>);
+        const int grid = occupancy_grid(k, threads, 0, work);
+        return launch_rc(launch_pdl(k, dim3((unsigned)grid), dim3(threads), 0, s, a), "xor_stream_kernel");
       }
       return a.nin <= 3 ? launch_xor<4>(a, s, 2 * kLRingBytes) : launch_xor<1>(a, s, kLRingBytes);
     case Field::GF8: {
