@@ -269,6 +269,26 @@ int gsec_parity_bytes(const gsec_code* code, int64_t data_bytes, int64_t* out) {
   return GSEC_OK;
 }
 
+namespace {
+// True if any of the pointers lies in another GPU's memory (a peer buffer
+// mapped with gsec_ipc_import): such inputs are read by the bulk-copy kernels,
+// which keep more bytes in flight over NVLink than 16-byte loads do.
+bool any_remote(const void* const* p, int n) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  for (int i = 0; i < n; ++i) {
+    if (p[i] == nullptr) continue;
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p[i]) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (attr.type == cudaMemoryTypeDevice && attr.device != dev) return true;
+  }
+  return false;
+}
+}  // namespace
+
 int gsec_encode(const gsec_code* code, const void* const* data_lo, const void* const* data_hi, int64_t split,
                 int64_t data_bytes, void* const* parity, int64_t begin, int64_t end, gsec_stream_t stream) {
   int rc = check_code(code);
@@ -305,6 +325,7 @@ int gsec_encode(const gsec_code* code, const void* const* data_lo, const void* c
     a.s_end = (end + sb - 1) / sb;
     a.k = k;
     a.p = code->p;
+    if (code->p <= 3) a.remote = any_remote(data_lo, k) || (two_seg && any_remote(data_hi, k));
     return rdp_encode(a, s);
   }
 
@@ -325,6 +346,7 @@ int gsec_encode(const gsec_code* code, const void* const* data_lo, const void* c
     a.out_end[j] = end;
     for (int i = 0; i < k; ++i) a.coef[j][i] = rs8_gen(k, k + j, i);
   }
+  if (a.field == Field::XOR && k <= 3) a.remote = any_remote(data_lo, k) || (two_seg && any_remote(data_hi, k));
   return run_linear(a, s);
 }
 
@@ -392,6 +414,15 @@ int gsec_decode(const gsec_code* code, void* const* shard_lo, void* const* shard
       a.out_hi[e] = hi(erased[e]);
     }
     rdp_build_program(a);
+    if (code->p <= 3) {
+      std::vector<const void*> in;
+      for (int i = 0; i < n; ++i)
+        if (!is_erased[i]) {
+          in.push_back(lo(i));
+          in.push_back(hi(i));
+        }
+      a.remote = any_remote(in.data(), (int)in.size());
+    }
     return rdp_decode(a, s);
   }
 
@@ -411,6 +442,11 @@ int gsec_decode(const gsec_code* code, void* const* shard_lo, void* const* shard
     a.out_lo[0] = lo(erased[0]);
     a.out_hi[0] = hi(erased[0]);
     a.out_end[0] = erased[0] < k ? data_bytes : end;
+    if (a.nin <= 3) {
+      std::vector<const void*> in(a.in_lo, a.in_lo + a.nin);
+      in.insert(in.end(), a.in_hi, a.in_hi + a.nin);
+      a.remote = any_remote(in.data(), (int)in.size());
+    }
     return run_linear(a, s);
   }
 

@@ -696,7 +696,7 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
     case Field::XOR:
       // measured: 2-3 inputs run best with 4 KiB stages and a 36 KiB ring, one
       // input with 4 KiB stages and the default ring, more inputs with 1 KiB stages
-      if (a.nin <= GSEC_XOR_STREAM_MAXIN) {
+      if (a.nin <= GSEC_XOR_STREAM_MAXIN && !a.remote) {  // peer inputs: bulk copies over NVLink are faster
         const int threads = 256;
         const int64_t work = (((a.end - a.begin) >> 4) + 3) / 4;
         auto k = a.nin == 1 ? xor_stream_kernel<1> : (a.nin == 2 ? xor_stream_kernel<2> : xor_stream_kernel<3>);

@@ -30,7 +30,7 @@ struct LinearPass {
   int nin;
   int nout;
   Field field;
-  uint32_t unity = 1;  // always 1; read from the launch parameters, so the compiler cannot fold it
+  int remote = 0;     // some input lies in another GPU's memory (read over NVLink)
 };
 
 // One launch that copies src[0..copy_len) to dst (bytes in [skip_lo, skip_hi)

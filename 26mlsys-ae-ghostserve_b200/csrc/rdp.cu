@@ -421,7 +421,9 @@ constexpr int kCtasPerSm = GSEC_RDP_CTAS;  // resident CTAs per SM (at most)
 // 16-byte lane of a stripe with all its cells' loads in flight, beat the
 // staging ring, whose per-item hand-offs dominate such short items (decode of
 // 16 MiB shards: 0.60 -> 1.07 of the copy peak, 64 MiB: 0.70 -> 0.91; encode
-// of 2 MiB shards 0.50 -> 0.61). From p = 5 on the ring is faster.
+// of 2 MiB shards 0.50 -> 0.61). From p = 5 on the ring is faster, and so it
+// is for inputs in another GPU's memory (bulk copies over NVLink outrun
+// 16-byte loads there).
 #ifndef GSEC_RDP_REG_DECODE_MAXP
 #define GSEC_RDP_REG_DECODE_MAXP 3
 #endif
@@ -430,7 +432,7 @@ constexpr int kCtasPerSm = GSEC_RDP_CTAS;  // resident CTAs per SM (at most)
 #endif
 template <int P>
 int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
-  if (a.unit % kSeg == 0 && P > GSEC_RDP_REG_ENCODE_MAXP) {  // TMA ring: units split into whole 1 KiB segments
+  if (a.unit % kSeg == 0 && (P > GSEC_RDP_REG_ENCODE_MAXP || a.remote)) {  // TMA ring: units split into whole 1 KiB segments
     LaunchCache& cache = launch_cache();
     auto k = rdp_encode_tma_kernel<P>;
     // small k makes small stages: keep ~18 KiB of loads in flight per CTA all the same
@@ -454,7 +456,7 @@ int launch_encode(const RdpEncodeArgs& a, cudaStream_t s) {
 }
 template <int P>
 int launch_decode(const RdpDecodeArgs& a, cudaStream_t s) {
-  if (a.unit % kSeg == 0 && P > GSEC_RDP_REG_DECODE_MAXP) {
+  if (a.unit % kSeg == 0 && (P > GSEC_RDP_REG_DECODE_MAXP || a.remote)) {
     LaunchCache& cache = launch_cache();
     auto k = rdp_decode_tma_kernel<P>;
     const int nalive = __builtin_popcount(a.alive);

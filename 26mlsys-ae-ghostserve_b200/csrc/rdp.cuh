@@ -17,6 +17,7 @@ struct RdpEncodeArgs {
   int64_t s_begin, s_end;  // stripe range
   int k;
   int p;
+  int remote = 0;       // some input lies in another GPU's memory (read over NVLink)
 };
 
 struct RdpDecodeArgs {
@@ -40,6 +41,7 @@ struct RdpDecodeArgs {
   int64_t unit;
   int64_t s_begin, s_end;
   int p;
+  int remote = 0;        // some input lies in another GPU's memory (read over NVLink)
 };
 
 bool rdp_prime_supported(int p);
