@@ -548,15 +548,20 @@ __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
   uint32_t len;
   // prologue: the first kGStages chunks of this CTA in flight
   int64_t it = blockIdx.x;
+  int64_t issued = 0;  // this CTA's chunks whose loads have been issued, in order
   for (int st = 0; st < kGStages && it + (int64_t)st * gridDim.x < items; ++st) {
     gather_item(a, it + (int64_t)st * gridDim.x, src, dst, len);
     pipe::bar_expect_tx(full + st, len);
     pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
+    ++issued;
   }
   for (int64_t k = 0; it < items; ++k, it += gridDim.x) {
     const int st = (int)(k % kGStages);
     if (!pipe::bar_wait(full + st, (uint32_t)((k / kGStages) & 1))) {
       atomicOr(&g_gather_status, 1u);
+      // let the loads still in flight land (bounded) before the CTA's shared memory goes away
+      for (int64_t q = k + 1; q < issued; ++q)
+        (void)pipe::bar_wait(full + q % kGStages, (uint32_t)((q / kGStages) & 1));
       break;
     }
     gather_item(a, it, src, dst, len);
@@ -568,6 +573,7 @@ __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
       gather_item(a, next, src, dst, len);
       pipe::bar_expect_tx(full + st, len);
       pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
+      ++issued;
     }
   }
   pipe::bulk_wait_all();
