@@ -513,22 +513,35 @@ constexpr int kGStages = 4;
 struct GatherArgs {
   const char* src[kGatherMax];
   int64_t bytes[kGatherMax];
-  int64_t item_end[kGatherMax];  // cumulative chunk counts
   int64_t dst_off[kGatherMax];   // byte offset of source i in dst
+  int64_t items;                 // (largest source's chunk count) x n
   int n;
   char* dst;
 };
 
+// Items interleave the sources (item it = chunk it / n of source it % n), so
+// the CTAs read every source at once, as the encode kernels read every shard
+// of a stripe at once: with peers as sources, all peer links carry traffic
+// together. An item past its source's end is empty (len = 0).
 __device__ __forceinline__ void gather_item(const GatherArgs& a, int64_t it, const char*& src, char*& dst,
                                             uint32_t& len) {
-  int i = 0;
-  while (i + 1 < a.n && it >= a.item_end[i]) ++i;
-  const int64_t c = it - (i ? a.item_end[i - 1] : 0);
-  const int64_t off = c * kGChunk;
+  const int i = (int)(it % a.n);
+  const int64_t off = (it / a.n) * kGChunk;
   const int64_t rest = a.bytes[i] - off;
-  len = (uint32_t)(rest < kGChunk ? rest : kGChunk);
+  len = (uint32_t)(rest <= 0 ? 0 : (rest < kGChunk ? rest : kGChunk));
   src = a.src[i] + off;
   dst = a.dst + a.dst_off[i] + off;
+}
+
+// Load one chunk into a stage; an empty chunk completes the stage's phase
+// with a plain arrival, so the ring's phase order stays the same.
+__device__ __forceinline__ void issue_chunk(unsigned char* stage, const char* src, uint32_t len, uint64_t* bar) {
+  if (len == 0) {
+    pipe::bar_arrive(bar);
+    return;
+  }
+  pipe::bar_expect_tx(bar, len);
+  pipe::bulk_load(stage, src, len, bar);
 }
 
 __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
@@ -542,7 +555,7 @@ __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
   grid_dep_wait();
   grid_dep_launch();
   if (threadIdx.x != 0) return;
-  const int64_t items = a.item_end[a.n - 1];
+  const int64_t items = a.items;
   const char* src;
   char* dst;
   uint32_t len;
@@ -551,8 +564,7 @@ __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
   int64_t issued = 0;  // this CTA's chunks whose loads have been issued, in order
   for (int st = 0; st < kGStages && it + (int64_t)st * gridDim.x < items; ++st) {
     gather_item(a, it + (int64_t)st * gridDim.x, src, dst, len);
-    pipe::bar_expect_tx(full + st, len);
-    pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
+    issue_chunk(smem + st * kGChunk, src, len, full + st);
     ++issued;
   }
   for (int64_t k = 0; it < items; ++k, it += gridDim.x) {
@@ -565,14 +577,15 @@ __global__ void __launch_bounds__(32) gather_bulk(const GatherArgs a) {
       break;
     }
     gather_item(a, it, src, dst, len);
-    pipe::bulk_store(dst, smem + st * kGChunk, len);
-    pipe::bulk_commit();
+    if (len > 0) {
+      pipe::bulk_store(dst, smem + st * kGChunk, len);
+      pipe::bulk_commit();
+    }
     const int64_t next = it + (int64_t)kGStages * gridDim.x;
     if (next < items) {
       pipe::bulk_wait_read_all();  // the stage's store has read it: refill
       gather_item(a, next, src, dst, len);
-      pipe::bar_expect_tx(full + st, len);
-      pipe::bulk_load(smem + st * kGChunk, src, len, full + st);
+      issue_chunk(smem + st * kGChunk, src, len, full + st);
       ++issued;
     }
   }
@@ -588,7 +601,7 @@ int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, 
   GatherArgs a{};
   a.n = n;
   a.dst = static_cast<char*>(dst);
-  int64_t items = 0, off = 0;
+  int64_t chunks = 0, off = 0;
   for (int i = 0; i < n; ++i) {
     if (bytes[i] < 0 || (bytes[i] & 15) || (bytes[i] && (!src[i] || !aligned16(src[i])))) {
       set_error("gather: source %d must be 16-byte aligned with a size that is a multiple of 16", i);
@@ -598,9 +611,11 @@ int copy_gather(const void* const* src, const int64_t* bytes, int n, void* dst, 
     a.bytes[i] = bytes[i];
     a.dst_off[i] = off;
     off += bytes[i];
-    items += (bytes[i] + kGChunk - 1) / kGChunk;
-    a.item_end[i] = items;
+    const int64_t c = (bytes[i] + kGChunk - 1) / kGChunk;
+    chunks = c > chunks ? c : chunks;
   }
+  const int64_t items = chunks * n;
+  a.items = items;
   if (items == 0) return GSEC_OK;
   if (!dst || !aligned16(dst)) {
     set_error("gather: destination must be 16-byte aligned");
