@@ -21,9 +21,12 @@ Modules
                prime and stripe units, and Reed-Solomon over GF(2^8)/0x11d with a
                Cauchy generator.  There is no reference implementation to run, so
                these are pinned by hand-checkable known-answer vectors, algebraic
-               properties (MDS: every <= m erasure pattern decodes) and a
-               decoder written independently of the CUDA decoder (peeling over
-               row/diagonal equations, versus precomputed syndrome masks).
+               properties (MDS: every <= m erasure pattern decodes), a decoder
+               written independently of the CUDA decoder (peeling over
+               row/diagonal equations, versus precomputed syndrome masks), and
+               the SHA-256 digests of a second, independent restatement
+               (``tests/golden/kat.py``: bitwise field arithmetic, a diagonal walk)
+               committed in ``tests/golden/kat_codes.json``.
 ``cpu``        C/OpenMP restatement used as the timed CPU baseline (built by
                ``oracle/cpu/Makefile`` into ``oracle/cpu/liboracle.so``).
 ``build_ref``  recipe that compiles the reference's CUDA extensions into
