@@ -11,7 +11,13 @@
 // tables), so one shared-memory load serves every parity shard.  Each table is
 // replicated R times and lane l reads copy l % R: with R = 32 the 32 lanes of a
 // warp always hit 32 different banks whatever the data bytes are.
+//
+// The RS(k, m <= 2) encode itself (coefficients = the Cauchy generator) skips
+// the tables: gf8_cauchy_kernel transposes 32-byte groups into bit planes and
+// runs the generator as a compile-time XOR network (cauchy_net.cuh), about 60 %
+// of the table kernel's instructions per byte.
 #include "linear.cuh"
+#include "cauchy_net.cuh"
 #include "pipe.cuh"
 
 namespace gsec {
@@ -299,6 +305,102 @@ __global__ void __launch_bounds__(1024) gf8_fixed_kernel(const LinearPass a) {
   if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
 }
 
+// ------------------------------------ GF(2^8) encode, generator fixed at build
+// Multiplying a byte by a constant c is a linear map over GF(2): bit r of c*x is
+// the XOR of the bits s of x for which bit r of c*2^s is set. With the 32 bytes
+// of a group transposed into 8 bit planes (word s = bit s of every byte), one
+// output plane is a plain XOR of input planes, and with the code's generator
+// known at compile time the choice of planes is a constant: the network
+// (cauchy_net.cuh, written by gen_cauchy_net.py with the XOR pairs that several
+// planes share computed once) is straight-line 3-input XORs, no tables, no
+// lookups. Per 32-byte group of one input, its 8x8 bit transpose in every byte
+// lane of 8 words (its own inverse) takes 60 integer instructions; the network
+// takes about 0.65 per input byte for two parity rows. The generator is the Cauchy block C[j][i] = 1 / ((k + j) XOR i) over
+// GF(2^8)/0x11d that the engine's RS(k, m) encode uses; passes with other
+// coefficients (decode) keep the table kernel.
+__host__ __device__ constexpr uint32_t cx_gf8_mul(uint32_t a, uint32_t b) {
+  uint32_t acc = 0;
+  while (b) {
+    if (b & 1u) acc ^= a;
+    a <<= 1;
+    if (a & 0x100u) a ^= 0x11du;
+    b >>= 1;
+  }
+  return acc;
+}
+__host__ __device__ constexpr uint32_t cx_gf8_inv(uint32_t a) {  // a^254 (a != 0)
+  uint32_t r = 1, e = 254;
+  while (e) {
+    if (e & 1u) r = cx_gf8_mul(r, a);
+    a = cx_gf8_mul(a, a);
+    e >>= 1;
+  }
+  return r;
+}
+__host__ __device__ constexpr uint32_t cauchy_coef(int k, int j, int i) {
+  return cx_gf8_inv((uint32_t)((k + j) ^ i));
+}
+// Exchange the bits of a under (m << s) with the bits of b under m.
+__device__ __forceinline__ void swap_bits(uint32_t& a, uint32_t& b, int s, uint32_t m) {
+  const uint32_t x = ((a >> s) ^ b) & m;
+  b ^= x;
+  a ^= x << s;
+}
+// Bit t of byte lane l of word s  <->  bit s of byte lane l of word t.
+__device__ __forceinline__ void transpose8(uint32_t (&w)[8]) {
+#pragma unroll
+  for (int t = 0; t < 4; ++t) swap_bits(w[t], w[t + 4], 4, 0x0f0f0f0fu);
+#pragma unroll
+  for (int t = 0; t < 8; t += (t & 1) ? 3 : 1) swap_bits(w[t], w[t + 2], 2, 0x33333333u);
+#pragma unroll
+  for (int t = 0; t < 8; t += 2) swap_bits(w[t], w[t + 1], 1, 0x55555555u);
+}
+
+// FLAT: every shard is one segment and every output takes the whole range, so
+// a lane's two vectors of a shard sit 512 bytes apart behind one pointer and
+// no store needs a bound check (the bench's and the hook's encodes).
+template <int K, int M, bool FLAT>
+__global__ void __launch_bounds__(256, 3) gf8_cauchy_kernel(const LinearPass a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  // A warp takes 1 KiB of every shard at a time; lane l transposes its vectors
+  // l and l + 32 as one 32-byte group (any two vectors make a group), so every
+  // load and store instruction covers 512 contiguous bytes.
+  const int64_t nvec = (a.end - a.begin) >> 4;
+  const int64_t nchunk = (nvec + 63) >> 6;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarp = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunk; c += nwarp) {
+    const int64_t v0 = (c << 6) + lane;
+    if (v0 >= nvec) continue;  // the last chunk's idle lanes
+    const bool pair = v0 + 32 < nvec;
+    const int64_t off0 = a.begin + (v0 << 4), off1 = off0 + 512;
+    uint32_t w[K][8];
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      const char* p0 = FLAT ? a.in_lo[i] + off0 : seg(a.in_lo[i], a.in_hi[i], a.split, off0);
+      const char* p1 = FLAT ? p0 + 512 : seg(a.in_lo[i], a.in_hi[i], a.split, off1);
+      const uint4 x0 = ld16(p0);
+      const uint4 x1 = pair ? ld16(p1) : vzero();
+      w[i][0] = x0.x, w[i][1] = x0.y, w[i][2] = x0.z, w[i][3] = x0.w;
+      w[i][4] = x1.x, w[i][5] = x1.y, w[i][6] = x1.z, w[i][7] = x1.w;
+    }
+#pragma unroll
+    for (int i = 0; i < K; ++i) transpose8(w[i]);
+    uint32_t o[M][8];
+    CauchyNet<K, M>::run(w, o);
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+      transpose8(o[j]);
+      char* q0 = FLAT ? a.out_lo[j] + off0 : seg(a.out_lo[j], a.out_hi[j], a.split, off0);
+      char* q1 = FLAT ? q0 + 512 : seg(a.out_lo[j], a.out_hi[j], a.split, off1);
+      if (FLAT || off0 + 16 <= a.out_end[j]) st16(q0, make_uint4(o[j][0], o[j][1], o[j][2], o[j][3]));
+      if (pair && (FLAT || off1 + 16 <= a.out_end[j])) st16(q1, make_uint4(o[j][4], o[j][5], o[j][6], o[j][7]));
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) linear_tail(a, a.begin + (nvec << 4));
+}
+
 // --------------------------------------------------------------- GF(2^8) ----
 template <int NOUT, int R>
 __global__ void __launch_bounds__(1024) gf8_vec_kernel(const LinearPass a) {
@@ -513,6 +615,40 @@ int launch_gf8_fixed(const LinearPass& a, cudaStream_t s) {
   return launch_rc(launch_pdl(k, dim3(grid), dim3(threads), smem, s, a), "gf8_fixed_kernel");
 }
 
+template <int K, int M>
+int launch_gf8_cauchy(const LinearPass& a, cudaStream_t s) {
+  bool flat = a.split >= a.end;
+  for (int j = 0; j < M; ++j) flat = flat && a.out_end[j] >= a.end;
+  auto k = flat ? gf8_cauchy_kernel<K, M, true> : gf8_cauchy_kernel<K, M, false>;
+  const int threads = 256;
+  const int grid = occupancy_grid(k, threads, 0, ((((a.end - a.begin) >> 4) + 63) >> 6) * 32);
+  return launch_rc(launch_pdl(k, dim3((unsigned)grid), dim3(threads), 0, s, a), "gf8_cauchy_kernel");
+}
+
+// The compile-time network when the pass's coefficients are the Cauchy
+// generator's parity rows of RS(k, m) with 2 <= k, m <= 2, k + m <= 8; -1 when
+// they are not. (Measured: with three or four parity rows the network costs
+// more than the table kernel's lookups, which stay in use there.)
+int try_gf8_cauchy(const LinearPass& a, cudaStream_t s) {
+  for (int j = 0; j < a.nout; ++j)
+    for (int i = 0; i < a.nin; ++i)
+      if (a.coef[j][i] != cauchy_coef(a.nin, j, i)) return -1;
+  switch (a.nin * 8 + a.nout) {
+    case 2 * 8 + 1: return launch_gf8_cauchy<2, 1>(a, s);
+    case 2 * 8 + 2: return launch_gf8_cauchy<2, 2>(a, s);
+    case 3 * 8 + 1: return launch_gf8_cauchy<3, 1>(a, s);
+    case 3 * 8 + 2: return launch_gf8_cauchy<3, 2>(a, s);
+    case 4 * 8 + 1: return launch_gf8_cauchy<4, 1>(a, s);
+    case 4 * 8 + 2: return launch_gf8_cauchy<4, 2>(a, s);
+    case 5 * 8 + 1: return launch_gf8_cauchy<5, 1>(a, s);
+    case 5 * 8 + 2: return launch_gf8_cauchy<5, 2>(a, s);
+    case 6 * 8 + 1: return launch_gf8_cauchy<6, 1>(a, s);
+    case 6 * 8 + 2: return launch_gf8_cauchy<6, 2>(a, s);
+    case 7 * 8 + 1: return launch_gf8_cauchy<7, 1>(a, s);
+    default: return -1;
+  }
+}
+
 template <int NOUT>
 int dispatch_gf8(const LinearPass& a, int r, cudaStream_t s) {
   switch (r) {
@@ -705,6 +841,10 @@ int run_linear(const LinearPass& a, cudaStream_t s) {
       }
       return a.nin <= 3 ? launch_xor<4>(a, s, 2 * kLRingBytes) : launch_xor<1>(a, s, kLRingBytes);
     case Field::GF8: {
+      if (a.nin >= 2 && a.nout >= 1) {
+        const int rc = try_gf8_cauchy(a, s);
+        if (rc >= 0) return rc;
+      }
       switch (a.nin) {
         case 1: return launch_gf8_fixed<1>(a, s);
         case 2: return launch_gf8_fixed<2>(a, s);

@@ -400,7 +400,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu / peak, 4), "traffic": traffic_from_profiles(tag),
                 "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
-                "kernel": ({"rdp": "rdp_encode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
+                "kernel": ({"rdp": "rdp_encode_tma_kernel<7>", "rs8": "gf8_cauchy_kernel<6,2,flat>", "xor": "xor_tma_kernel"}
                            if args.op == "encode" else
                            {"rdp": "rdp_decode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
                            )[wl["scheme"]]}
