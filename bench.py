@@ -402,7 +402,7 @@ def main():
                 "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
                 "kernel": ({"rdp": "rdp_encode_tma_kernel<7>", "rs8": "gf8_cauchy_kernel<6,2,flat>", "xor": "xor_tma_kernel"}
                            if args.op == "encode" else
-                           {"rdp": "rdp_decode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6>", "xor": "xor_tma_kernel"}
+                           {"rdp": "rdp_decode_tma_kernel<7>", "rs8": "gf8_fixed_kernel<6,false>", "xor": "xor_tma_kernel"}
                            )[wl["scheme"]]}
     if world > 1:
         if args.op == "decode":  # the decode reads the survivors only

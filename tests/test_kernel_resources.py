@@ -18,7 +18,8 @@ CSRC = os.path.join(ROOT, "26mlsys-ae-ghostserve_b200", "csrc")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 HOT = [r"rdp_encode_tma_kernelILi7E", r"rdp_decode_tma_kernelILi7E", r"xor_tma_kernelILi1E",
-       r"xor_tma_kernelILi4E"] + [rf"gf8_fixed_kernelILi{k}E" for k in range(2, 9)] + \
+       r"xor_tma_kernelILi4E"] + [rf"gf8_fixed_kernelILi{k}ELb0E" for k in range(2, 9)] + \
+      [rf"gf8_fixed_kernelILi{k}ELb1E" for k in (4, 5)] + \
       [rf"gf8_cauchy_kernelILi{k}ELi{m}ELb{f}E" for k in range(2, 8) for m in (1, 2) if k + m <= 8 for f in (0, 1)]
 
 
