@@ -10,7 +10,9 @@ TP=8 (K and V [32 layers, 2048 tokens, 1 kv-head, 128] bf16 ~ N(0,1), seeded):
 A step = one encode of that codeword.  ``value`` is algorithmic bytes
 ((k+m) shards: k*32 MiB read + 2 parity shards written) / device time, summed
 over ranks.  ``e2e`` runs the same step through the host pipeline (pinned host
-shards -> H2D -> encode -> D2H parity), copies inside the timed region.
+shards -> H2D -> encode -> D2H parity), copies inside the timed region; with N
+ranks each rank encodes its own codeword from its own pinned host buffers (one
+PCIe link per GPU), timed together, max over ranks.
 
 N GPUs (torchrun): each rank owns one codeword whose six data shards live on
 six different GPUs (shard j of rank c's codeword on GPU (c + j) mod N, j = 0
@@ -413,8 +415,12 @@ def main():
         roofline["bound"] = "nvlink" if remote_bytes / 900e9 > (alg_bytes - remote_bytes) / (peak * 1e9) else "hbm"
 
     e2e = None
-    if not args.no_e2e and world == 1 and args.op == "encode":
-        e2e = measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, max(3, min(args.steps, 20)))
+    if not args.no_e2e and args.op == "encode":
+        barrier()
+        e2e = measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, max(3, min(args.steps, 20)),
+                          want_digests=rec["parity_sha256"], world=world,
+                          rendezvous=(lambda: dist.all_reduce(torch.ones(1, device=device))) if world > 1 else None,
+                          max_over_ranks=max_over_ranks if world > 1 else None)
 
     cpu_baseline = None
     if not args.no_cpu_baseline and rank == 0 and world == 1 and args.op == "encode":
@@ -1174,8 +1180,14 @@ def measure_recovery(torch, dist, model, ft, args, device, variant):
     return out
 
 
-def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):
-    """Same step through the host pipeline: pinned host shards in, parity out."""
+def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps, want_digests=None, world=1,
+                rendezvous=None, max_over_ranks=None):
+    """Same step through the host pipeline: pinned host shards in, parity out.
+
+    With N ranks every rank encodes its own codeword from its own pinned host
+    buffers (host-resident shards have no reason to be spread over GPUs), the
+    ranks' timed steps start together (stream-ordered rendezvous), the time is
+    the max over ranks, and the value is the N codewords' bytes over it."""
     off = __import__(PKG + ".offload", fromlist=["HostPipeline"])
     host_data = [torch.empty(nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(spec.k)]
     for h, d in zip(host_data, slots):
@@ -1185,8 +1197,12 @@ def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):
     for _ in range(2):
         pipe.encode(host_data, host_par)
     torch.cuda.synchronize()
+    for h in host_par:
+        h.zero_()  # the check below sees the timed steps' parity only
     pipe.launches = 0
     stream = torch.cuda.current_stream()
+    if rendezvous is not None:
+        rendezvous()  # on the stream; the pipeline's first copies wait for it
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(steps):  # consecutive steps overlap; the last joins the timing stream
@@ -1194,11 +1210,18 @@ def measure_e2e(torch, g, spec, slots, nbytes, pbytes, alg_bytes, steps):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    return {"value": round(alg_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": spec.k * nbytes, "d2h_bytes_per_step": spec.m * pbytes,
-            "ms_per_step": round(ms, 4), "steps": steps, "gpu_launches_per_step": pipe.launches // steps,
-            "path": "offload.HostPipeline: pinned host -> H2D -> gsec_encode -> D2H, 8 MiB chunks on 3 streams, "
-                    "consecutive steps overlapped"}
+    if max_over_ranks is not None:
+        ms = max_over_ranks(ms)
+    out = {"value": round(alg_bytes * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": spec.k * nbytes * world, "d2h_bytes_per_step": spec.m * pbytes * world,
+           "ms_per_step": round(ms, 4), "steps": steps, "gpu_launches_per_step": pipe.launches // steps,
+           "path": "offload.HostPipeline: pinned host -> H2D -> gsec_encode -> D2H, 8 MiB chunks on 3 streams, "
+                   "consecutive steps overlapped" +
+                   ("; every rank its own codeword from its own pinned host buffers" if world > 1 else "")}
+    if want_digests is not None:
+        ok = [hashlib_np(h.numpy()) for h in host_par] == want_digests
+        out["verified"] = (max_over_ranks(0.0 if ok else 1.0) == 0.0) if max_over_ranks is not None else ok
+    return out
 
 
 if __name__ == "__main__":
